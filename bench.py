@@ -1,0 +1,339 @@
+"""Decode throughput of the Llama-3.2-1B F16 hot path on B200.
+
+Workload (one "step"): batch-1 greedy decode of the random-init
+Llama-3.2-1B architecture -- 31 decode forwards at positions 16..46 after a
+16-token prompt (the 32-token greedy run of the reference's headline config;
+the prompt prefill and the first generated token happen once, untimed).
+All 31 forwards run in ONE launch of the fused decode kernel.
+
+  value  device time of the fused launch (CUDA events), inputs resident
+  e2e    the public C-ABI call lc_decode per step: host token in, host token
+         ids out (pinned copies inside the timed region)
+  --impl reference   the oracle (C restatement of the reference's
+                     PlainJavaKernelFactory path) on the host cores
+
+Multi-GPU (torchrun): one independent sequence per GPU (replicas, no
+collective on the data path); value = sequences x tokens / max-over-ranks time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "llama3-java-hat_b200")]
+
+import numpy as np  # noqa: E402
+
+METRIC = "decode tok/s @1B F16 batch1"
+PROMPT_LEN = 16
+NEW_TOKENS = 32
+DECODE_STEPS = NEW_TOKENS - 1  # forwards after the first generated token
+SEED = 1234
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ------------------------------------------------------------- clocks ----
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------- roofline ----
+
+def algorithmic_bytes(cfg, positions) -> int:
+    """Bytes one decode launch must move at minimum (per position: every weight
+    once, norm vectors, the embedding row, KV write + KV read of positions
+    0..pos, the logits write)."""
+    total = 0
+    kv_row = cfg.n_layers * 2 * cfg.kv_dim * 4
+    for pos in positions:
+        total += cfg.weight_bytes()
+        total += (2 * cfg.n_layers + 1) * cfg.dim * 4
+        total += cfg.dim * 2
+        total += kv_row + kv_row * (pos + 1)
+        total += cfg.vocab * 4
+    return total
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def committed_traffic():
+    """DRAM bytes per launch of the fused decode kernel from the committed ncu
+    summary (profiles/decode_kernel_traffic.json), or None."""
+    p = os.path.join(ROOT, "profiles", "decode_kernel_traffic.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d
+    except (OSError, ValueError):
+        return None
+
+
+# -------------------------------------------------------- CPU baseline ----
+
+def cpu_sample(cfg, w, prompt, threads: int, budget_s: float):
+    """Oracle forwards (the C restatement of the reference path) on the host:
+    decode forwards at positions 0,1,2,... until `budget_s` is spent (at least
+    2).  Per-forward cost is dominated by the 2.47 GB weight stream, so these
+    positions stand for the timed decode positions."""
+    from oracle import oracle as O
+    O.build()
+    O.set_threads(threads)
+    om = O.OracleModel(cfg, w)
+    om.forward(int(prompt[0]), 0)  # warm page cache / tables
+    n, t0 = 0, time.perf_counter()
+    while True:
+        om.forward(int(prompt[n % len(prompt)]), n)
+        n += 1
+        el = time.perf_counter() - t0
+        if n >= 2 and el >= budget_s:
+            break
+    return n, el
+
+
+# --------------------------------------------------------------- main ----
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    from llamahat.config import LLAMA_3_2_1B
+    from llamahat.synth import synth_prompt, synth_weights
+    from oracle import oracle as O
+    O.build()
+    cfg = LLAMA_3_2_1B
+    w = synth_weights(cfg, seed=SEED)
+    prompt = synth_prompt(PROMPT_LEN, seed=SEED)
+    threads = O.max_threads()
+    O.set_threads(threads)
+    om = O.OracleModel(cfg, w)
+    per_step = max(1, int(os.environ.get("BENCH_REF_FORWARDS", "2")))
+    times = []
+    pos = 0
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        for _ in range(per_step):
+            om.forward(int(prompt[pos % PROMPT_LEN]), pos)
+            pos += 1
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            times.append(dt)
+    tot = sum(times)
+    value = per_step * len(times) / tot
+    sample = (f"{per_step} oracle decode forwards per step at KV positions < {pos} "
+              f"(C restatement of PlainJavaKernelFactory; no JDK on this host)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * tot / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(),
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config():
+    return {"workload": "Llama-3.2-1B random-init F16 (seed 1234), 16-token prompt, greedy decode; one step = "
+                        "31 decode forwards (positions 16..46) in one fused launch",
+            "model": "llama-3.2-1b-arch", "batch": 1, "prompt_tokens": PROMPT_LEN, "decode_forwards": DECODE_STEPS,
+            "global_batch": None, "seq_len": PROMPT_LEN + NEW_TOKENS - 1, "parallelism": "replicas",
+            "l2": "weights 2.47 GB per forward > 126 MB L2: inputs larger than L2, no flush"}
+
+
+def run_ours(args):
+    import torch
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    import llamahat
+    from llamahat.config import LLAMA_3_2_1B
+    from llamahat.synth import synth_prompt, synth_weights
+
+    cfg = LLAMA_3_2_1B
+    t0 = time.perf_counter()
+    w = synth_weights(cfg, seed=SEED)
+    log(f"[rank {rank}] weights generated in {time.perf_counter() - t0:.1f}s")
+    acc = llamahat.Accelerator(local)
+    model = llamahat.CudaModel(cfg, w, acc=acc)
+    sess = llamahat.Session(model)
+    prompt = synth_prompt(PROMPT_LEN, seed=SEED + rank)
+    first = sess.generate(prompt, 1, stop=())  # prefill + first token (untimed)
+    tok0 = int(first[0])
+    out = np.zeros(DECODE_STEPS, np.int32)
+    stream = torch.cuda.ExternalStream(acc.stream, device=torch.device("cuda", local))
+
+    # warm-up
+    for _ in range(args.warmup):
+        sess.decode(tok0, PROMPT_LEN, DECODE_STEPS, out)
+    ref_tokens = out.copy()
+
+    # device-resident timing: CUDA events around each fused launch
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launch_ms = []
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            sess.decode(tok0, PROMPT_LEN, DECODE_STEPS, out)
+            launch_ms.append(sess.last_ms())
+        torch.cuda.synchronize()
+        # e2e: events on the library stream bracketing the public calls
+        # (pinned token H2D, launch, token ids D2H, host sync -- every step)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            sess.decode(tok0, PROMPT_LEN, DECODE_STEPS, out)
+        e1.record(stream)
+        e1.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    assert np.array_equal(out, ref_tokens), "decode is not deterministic"
+
+    dev_ms = sum(launch_ms) / len(launch_ms)
+    if dist:
+        t = torch.tensor([dev_ms, e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms, e2e_ms = float(t[0]), float(t[1])
+    n = ws
+    value = n * DECODE_STEPS / (dev_ms / 1000.0)
+    e2e_value = n * DECODE_STEPS / (e2e_ms / 1000.0)
+
+    line = None
+    if rank == 0:
+        positions = range(PROMPT_LEN, PROMPT_LEN + DECODE_STEPS)
+        alg = algorithmic_bytes(cfg, positions)
+        peak, peak_kind = measured_peak()
+        achieved = alg / (dev_ms / 1000.0) / 1e9
+        tr = committed_traffic()
+        roof = {"bound": "hbm", "kernel": "decode_kernel<8>", "achieved": achieved, "peak": peak,
+                "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})", "unit": "GB/s",
+                "frac": achieved / peak, "algorithmic_bytes_per_launch": alg,
+                "traffic": tr.get("dram_bytes_per_launch") if tr else None,
+                "traffic_source": tr.get("source") if tr else None}
+        cpu = None
+        if not args.no_cpu_baseline:
+            try:
+                nf, el = cpu_sample(cfg, w, prompt, threads=1, budget_s=args.cpu_budget)
+                cpu = {"value": nf / el, "unit": "tok/s", "cores": 1, "kind": "port",
+                       "sample": f"{nf} oracle forwards (positions 0..{nf - 1}) on 1 host thread, {el:.1f}s; "
+                                 "C restatement of PlainJavaKernelFactory (no JDK on the host)"}
+            except Exception as e:  # pragma: no cover - reported, not fatal
+                cpu = {"error": str(e)}
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": n, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "weights": "f16", "data": "synthetic",
+            "config": workload_config(), "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 4 * DECODE_STEPS, "ms_per_step": e2e_ms},
+            "gpu_launches": args.steps, "clocks": clk.summary(),
+            "per_forward_us": 1000.0 * dev_ms / DECODE_STEPS,
+        }
+    sess.close()
+    model.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,951 @@
+// lc_api.cu -- the extern "C" surface of libllamacuda.so (include/llamacuda.h).
+//
+// Host-side runtime: contexts (device + stream + staging pool), host-buffer
+// staging for the per-kernel operators, model weight storage and upload,
+// sessions (device-resident KV cache and activations) and the launches of the
+// fused decode kernel.  Nothing here computes model math on the CPU: every
+// operator runs a CUDA kernel, and a missing or failing kernel is an error.
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/llamacuda.h"
+#include "lc_attention.cuh"
+#include "lc_internal.h"
+
+using namespace lc;
+
+// ------------------------------------------------------------ errors ----
+
+static thread_local std::string g_last_error;
+
+static int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+static int cuda_fail(cudaError_t e, const char* what) {
+    return fail(e == cudaErrorMemoryAllocation ? LC_ERR_OUT_OF_MEMORY : LC_ERR_CUDA, "%s: %s (%s)", what,
+                cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define CK(call, what)                                   \
+    do {                                                 \
+        cudaError_t _e = (call);                         \
+        if (_e != cudaSuccess) return cuda_fail(_e, what); \
+    } while (0)
+
+extern "C" int lc_last_error(char* buf, size_t n) {
+    if (buf && n) {
+        size_t k = g_last_error.size() < n - 1 ? g_last_error.size() : n - 1;
+        memcpy(buf, g_last_error.data(), k);
+        buf[k] = 0;
+    }
+    return (int)g_last_error.size();
+}
+
+extern "C" int lc_abi_version(void) { return LLAMACUDA_ABI_VERSION; }
+
+namespace lc {
+void make_rope_freq(RopeFreq* out, float theta, int head_dim) {
+    memset(out, 0, sizeof(*out));
+    for (int i = 0; i < head_dim && i / 2 < 256; i += 2)
+        out->f[i / 2] = (float)(1.0 / pow((double)theta, (double)i / (double)head_dim));  // RoPE.java:42
+}
+}  // namespace lc
+
+// ----------------------------------------------------------- context ----
+
+struct lc_context {
+    int device = 0;
+    int sms = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<void*> pool;        // staging buffers, grow-only
+    std::vector<size_t> pool_bytes;
+    int* d_err = nullptr;           // device error word of standalone kernels
+    void* attn_scratch = nullptr;
+    size_t attn_scratch_bytes = 0;
+};
+
+extern "C" int lc_device_count(int* count) {
+    if (!count) return fail(LC_ERR_INVALID_ARG, "count is NULL");
+    CK(cudaGetDeviceCount(count), "cudaGetDeviceCount");
+    return LC_OK;
+}
+
+extern "C" int lc_context_create(int device, lc_context** out) {
+    if (!out) return fail(LC_ERR_INVALID_ARG, "out is NULL");
+    int n = 0;
+    CK(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+    if (device < 0 || device >= n) return fail(LC_ERR_INVALID_ARG, "device %d out of range [0,%d)", device, n);
+    CK(cudaSetDevice(device), "cudaSetDevice");
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    if (prop.major < 10) return fail(LC_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a", device, prop.major, prop.minor);
+    lc_context* c = new lc_context();
+    c->device = device;
+    c->sms = prop.multiProcessorCount;
+    cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&c->d_err, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        delete c;
+        return cuda_fail(e, "context setup");
+    }
+    *out = c;
+    return LC_OK;
+}
+
+extern "C" int lc_context_destroy(lc_context* c) {
+    if (!c) return LC_OK;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    for (void* p : c->pool) cudaFree(p);
+    if (c->attn_scratch) cudaFree(c->attn_scratch);
+    if (c->d_err) cudaFree(c->d_err);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+    return LC_OK;
+}
+
+static int check_device_error(lc_context* c) {
+    int h = 0;
+    CK(cudaMemcpy(&h, c->d_err, sizeof(int), cudaMemcpyDeviceToHost), "read device error word");
+    if (h != 0) {
+        cudaMemset(c->d_err, 0, sizeof(int));
+        return fail(LC_ERR_TIMEOUT, "device-side wait gave up (code %d)", h);
+    }
+    return LC_OK;
+}
+
+extern "C" int lc_context_synchronize(lc_context* c) {
+    if (!c) return fail(LC_ERR_INVALID_ARG, "context is NULL");
+    CK(cudaSetDevice(c->device), "cudaSetDevice");
+    CK(cudaStreamSynchronize(c->stream), "cudaStreamSynchronize");
+    return check_device_error(c);
+}
+
+extern "C" void* lc_context_stream(lc_context* c) { return c ? (void*)c->stream : nullptr; }
+extern "C" int lc_context_sm_count(lc_context* c) { return c ? c->sms : 0; }
+
+// ------------------------------------------------------------ staging ----
+//
+// Host pointers are copied into pooled device buffers; device pointers of the
+// context's device are used directly.  After the launch, staged outputs are
+// copied back and the call synchronises.
+
+namespace {
+
+enum Dir { kIn, kOut, kInOut };
+
+struct Stager {
+    lc_context* c;
+    int slot = 0;
+    bool any_host = false;
+    struct Back {
+        void* host;
+        void* dev;
+        size_t bytes;
+    };
+    std::vector<Back> backs;
+    int status = LC_OK;
+
+    explicit Stager(lc_context* ctx) : c(ctx) {}
+
+    bool is_device(const void* p, int* rc) {
+        cudaPointerAttributes a;
+        cudaError_t e = cudaPointerGetAttributes(&a, p);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
+            if (a.type == cudaMemoryTypeDevice && a.device != c->device) {
+                *rc = fail(LC_ERR_INVALID_ARG, "device pointer belongs to device %d, context is on %d", a.device, c->device);
+            }
+            return true;
+        }
+        return false;
+    }
+
+    void* buffer(size_t bytes) {
+        if ((size_t)slot >= c->pool.size()) {
+            c->pool.push_back(nullptr);
+            c->pool_bytes.push_back(0);
+        }
+        if (c->pool_bytes[slot] < bytes) {
+            if (c->pool[slot]) cudaFree(c->pool[slot]);
+            c->pool[slot] = nullptr;
+            c->pool_bytes[slot] = 0;
+            size_t want = bytes < 256 ? 256 : bytes;
+            if (cudaMalloc(&c->pool[slot], want) != cudaSuccess) {
+                cudaGetLastError();
+                return nullptr;
+            }
+            c->pool_bytes[slot] = want;
+        }
+        return c->pool[slot++];
+    }
+
+    // Returns the device pointer to hand to the kernel, or nullptr on error
+    // (status set).
+    void* arg(const void* p, size_t bytes, Dir d) {
+        if (status != LC_OK) return nullptr;
+        if (!p) {
+            status = fail(LC_ERR_INVALID_ARG, "NULL buffer");
+            return nullptr;
+        }
+        int rc = LC_OK;
+        if (is_device(p, &rc)) {
+            if (rc != LC_OK) status = rc;
+            return rc == LC_OK ? const_cast<void*>(p) : nullptr;
+        }
+        any_host = true;
+        void* dev = buffer(bytes);
+        if (!dev) {
+            status = fail(LC_ERR_OUT_OF_MEMORY, "staging buffer of %zu bytes", bytes);
+            return nullptr;
+        }
+        if (d != kOut && bytes) {
+            cudaError_t e = cudaMemcpyAsync(dev, p, bytes, cudaMemcpyHostToDevice, c->stream);
+            if (e != cudaSuccess) {
+                status = cuda_fail(e, "copy in");
+                return nullptr;
+            }
+        }
+        if (d != kIn) backs.push_back({const_cast<void*>(p), dev, bytes});
+        return dev;
+    }
+
+    int finish(cudaError_t launch) {
+        if (status != LC_OK) return status;
+        if (launch != cudaSuccess) return cuda_fail(launch, "kernel launch");
+        for (auto& b : backs) {
+            if (!b.bytes) continue;
+            cudaError_t e = cudaMemcpyAsync(b.host, b.dev, b.bytes, cudaMemcpyDeviceToHost, c->stream);
+            if (e != cudaSuccess) return cuda_fail(e, "copy out");
+        }
+        if (any_host) {
+            cudaError_t e = cudaStreamSynchronize(c->stream);
+            if (e != cudaSuccess) return cuda_fail(e, "synchronize");
+            return check_device_error(c);
+        }
+        return LC_OK;
+    }
+};
+
+}  // namespace
+
+#define CTX_CHECK(c)                                                        \
+    do {                                                                    \
+        if (!(c)) return fail(LC_ERR_INVALID_ARG, "context is NULL");       \
+        cudaError_t _e = cudaSetDevice((c)->device);                        \
+        if (_e != cudaSuccess) return cuda_fail(_e, "cudaSetDevice");       \
+    } while (0)
+
+// ------------------------------------------------------- per-kernel ops ----
+
+extern "C" int lc_gemv_f16(lc_context* c, const uint16_t* W, const float* x, float* y, int rows, int cols) {
+    CTX_CHECK(c);
+    if (rows <= 0 || cols <= 0) return fail(LC_ERR_INVALID_ARG, "rows=%d cols=%d", rows, cols);
+    Stager s(c);
+    auto* dW = (const uint16_t*)s.arg(W, (size_t)rows * cols * 2, kIn);
+    auto* dx = (const float*)s.arg(x, (size_t)cols * 4, kIn);
+    auto* dy = (float*)s.arg(y, (size_t)rows * 4, kOut);
+    if (s.status != LC_OK) return s.status;
+    cudaError_t e;
+    if (stream_gemv_supported(dW, dx, rows, cols)) {
+        e = launch_stream_gemv(dW, dx, dy, rows, cols, c->sms, c->d_err, c->stream);
+    } else {
+        launch_gemv_generic_f16(dW, dx, dy, rows, cols, c->stream);
+        e = cudaGetLastError();
+    }
+    return s.finish(e);
+}
+
+extern "C" int lc_gemv_f32(lc_context* c, const float* W, const float* x, float* y, int rows, int cols) {
+    CTX_CHECK(c);
+    if (rows <= 0 || cols <= 0) return fail(LC_ERR_INVALID_ARG, "rows=%d cols=%d", rows, cols);
+    Stager s(c);
+    auto* dW = (const float*)s.arg(W, (size_t)rows * cols * 4, kIn);
+    auto* dx = (const float*)s.arg(x, (size_t)cols * 4, kIn);
+    auto* dy = (float*)s.arg(y, (size_t)rows * 4, kOut);
+    if (s.status != LC_OK) return s.status;
+    launch_gemv_generic_f32(dW, dx, dy, rows, cols, c->stream);
+    return s.finish(cudaGetLastError());
+}
+
+extern "C" int lc_gemv_f16_batched(lc_context* c, const uint16_t* W, const float* X, float* Y, int rows, int cols,
+                                   int batch) {
+    CTX_CHECK(c);
+    if (rows <= 0 || cols <= 0 || batch <= 0) return fail(LC_ERR_INVALID_ARG, "rows=%d cols=%d batch=%d", rows, cols, batch);
+    Stager s(c);
+    auto* dW = (const uint16_t*)s.arg(W, (size_t)rows * cols * 2, kIn);
+    auto* dX = (const float*)s.arg(X, (size_t)batch * cols * 4, kIn);
+    auto* dY = (float*)s.arg(Y, (size_t)batch * rows * 4, kOut);
+    if (s.status != LC_OK) return s.status;
+    launch_gemv_batched_f16(dW, dX, dY, rows, cols, batch, c->stream);
+    return s.finish(cudaGetLastError());
+}
+
+extern "C" int lc_rmsnorm_rows(lc_context* c, float* x, const float* w, int rows, int width, float eps) {
+    CTX_CHECK(c);
+    if (rows <= 0 || width <= 0) return fail(LC_ERR_INVALID_ARG, "rows=%d width=%d", rows, width);
+    Stager s(c);
+    auto* dx = (float*)s.arg(x, (size_t)rows * width * 4, kInOut);
+    auto* dw = (const float*)s.arg(w, (size_t)width * 4, kIn);
+    if (s.status != LC_OK) return s.status;
+    launch_rmsnorm_rows(dx, dw, rows, width, eps, c->stream);
+    return s.finish(cudaGetLastError());
+}
+
+extern "C" int lc_rmsnorm(lc_context* c, float* x, const float* w, int size) {
+    return lc_rmsnorm_rows(c, x, w, 1, size, 1e-5f);  // RMSNorm.java:22
+}
+
+extern "C" int lc_rope_rows(lc_context* c, float* vec, const int32_t* pos, int rows, int num_heads, int head_dim,
+                            float theta) {
+    CTX_CHECK(c);
+    if (rows <= 0 || num_heads <= 0 || head_dim <= 0 || (head_dim & 1) || head_dim > 512)
+        return fail(LC_ERR_INVALID_ARG, "rows=%d num_heads=%d head_dim=%d", rows, num_heads, head_dim);
+    Stager s(c);
+    auto* dv = (float*)s.arg(vec, (size_t)rows * num_heads * head_dim * 4, kInOut);
+    auto* dp = (const int32_t*)s.arg(pos, (size_t)rows * 4, kIn);
+    if (s.status != LC_OK) return s.status;
+    RopeFreq fq;
+    make_rope_freq(&fq, theta, head_dim);
+    launch_rope_rows(dv, dp, rows, num_heads, head_dim, fq, c->stream);
+    return s.finish(cudaGetLastError());
+}
+
+extern "C" int lc_rope(lc_context* c, float* vec, int pos, int num_heads, int head_dim, float theta) {
+    CTX_CHECK(c);
+    if (num_heads <= 0 || head_dim <= 0 || (head_dim & 1) || head_dim > 512)
+        return fail(LC_ERR_INVALID_ARG, "num_heads=%d head_dim=%d", num_heads, head_dim);
+    // The position travels as a one-element array through the same kernel.
+    Stager s(c);
+    auto* dv = (float*)s.arg(vec, (size_t)num_heads * head_dim * 4, kInOut);
+    int32_t hp = pos;
+    auto* dp = (const int32_t*)s.arg(&hp, 4, kIn);
+    if (s.status != LC_OK) return s.status;
+    RopeFreq fq;
+    make_rope_freq(&fq, theta, head_dim);
+    launch_rope_rows(dv, dp, 1, num_heads, head_dim, fq, c->stream);
+    // hp is host memory, so the call is staged and finish() synchronises
+    // before this frame (and hp) goes away.
+    return s.finish(cudaGetLastError());
+}
+
+extern "C" int lc_silu(lc_context* c, float* x, int size) {
+    CTX_CHECK(c);
+    if (size <= 0) return fail(LC_ERR_INVALID_ARG, "size=%d", size);
+    Stager s(c);
+    auto* dx = (float*)s.arg(x, (size_t)size * 4, kInOut);
+    if (s.status != LC_OK) return s.status;
+    launch_silu(dx, size, c->stream);
+    return s.finish(cudaGetLastError());
+}
+
+extern "C" int lc_swiglu(lc_context* c, float* g, const float* u, int n) {
+    CTX_CHECK(c);
+    if (n <= 0) return fail(LC_ERR_INVALID_ARG, "n=%d", n);
+    Stager s(c);
+    auto* dg = (float*)s.arg(g, (size_t)n * 4, kInOut);
+    auto* du = (const float*)s.arg(u, (size_t)n * 4, kIn);
+    if (s.status != LC_OK) return s.status;
+    launch_swiglu(dg, du, n, c->stream);
+    return s.finish(cudaGetLastError());
+}
+
+extern "C" int lc_softmax_rows(lc_context* c, float* x, int rows, int width) {
+    CTX_CHECK(c);
+    if (rows <= 0 || width <= 0) return fail(LC_ERR_INVALID_ARG, "rows=%d width=%d", rows, width);
+    Stager s(c);
+    auto* dx = (float*)s.arg(x, (size_t)rows * width * 4, kInOut);
+    if (s.status != LC_OK) return s.status;
+    launch_softmax_rows(dx, rows, width, c->stream);
+    return s.finish(cudaGetLastError());
+}
+
+extern "C" int lc_softmax(lc_context* c, float* x, int size) { return lc_softmax_rows(c, x, 1, size); }
+
+extern "C" int lc_softmax_row(lc_context* c, float* x, int row_offset, int row_size) {
+    if (!x || row_offset < 0) return fail(LC_ERR_INVALID_ARG, "x=%p row_offset=%d", (void*)x, row_offset);
+    return lc_softmax_rows(c, x + row_offset, 1, row_size);
+}
+
+extern "C" int lc_attn_scores(lc_context* c, const float* q, const float* keys, float* scores, int seq_len,
+                              int head_dim) {
+    CTX_CHECK(c);
+    if (seq_len <= 0 || head_dim <= 0) return fail(LC_ERR_INVALID_ARG, "seq_len=%d head_dim=%d", seq_len, head_dim);
+    Stager s(c);
+    auto* dq = (const float*)s.arg(q, (size_t)head_dim * 4, kIn);
+    auto* dk = (const float*)s.arg(keys, (size_t)seq_len * head_dim * 4, kIn);
+    auto* ds = (float*)s.arg(scores, (size_t)seq_len * 4, kOut);
+    if (s.status != LC_OK) return s.status;
+    const float scale = 1.0f / (float)sqrt((double)head_dim);  // Attention.java:33
+    launch_attn_scores(dq, dk, ds, seq_len, head_dim, scale, c->stream);
+    return s.finish(cudaGetLastError());
+}
+
+extern "C" int lc_attn_values(lc_context* c, const float* p, const float* values, float* out, int seq_len,
+                              int head_dim) {
+    CTX_CHECK(c);
+    if (seq_len <= 0 || head_dim <= 0) return fail(LC_ERR_INVALID_ARG, "seq_len=%d head_dim=%d", seq_len, head_dim);
+    Stager s(c);
+    auto* dp = (const float*)s.arg(p, (size_t)seq_len * 4, kIn);
+    auto* dv = (const float*)s.arg(values, (size_t)seq_len * head_dim * 4, kIn);
+    auto* dout = (float*)s.arg(out, (size_t)head_dim * 4, kOut);
+    if (s.status != LC_OK) return s.status;
+    launch_attn_values(dp, dv, dout, seq_len, head_dim, c->stream);
+    return s.finish(cudaGetLastError());
+}
+
+extern "C" int lc_attention_decode(lc_context* c, const float* q, const float* k, const float* v, float* out,
+                                   const int32_t* seq_len, int batch, int n_heads, int n_kv_heads, int head_dim,
+                                   int64_t seq_stride, int64_t head_stride, int64_t pos_stride) {
+    CTX_CHECK(c);
+    if (batch <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads)
+        return fail(LC_ERR_INVALID_ARG, "batch=%d n_heads=%d n_kv_heads=%d", batch, n_heads, n_kv_heads);
+    if (head_dim != kAttnHeadDim) return fail(LC_ERR_UNSUPPORTED, "fused attention implements head_dim 64, got %d", head_dim);
+    if (n_heads / n_kv_heads > 8) return fail(LC_ERR_UNSUPPORTED, "at most 8 query heads per kv head");
+    if ((seq_stride | head_stride | pos_stride) & 3) return fail(LC_ERR_INVALID_ARG, "strides must be multiples of 4 floats");
+    // Lengths are needed on the host to size the split plan.
+    std::vector<int32_t> lens(batch);
+    {
+        cudaError_t e = cudaMemcpy(lens.data(), seq_len, (size_t)batch * 4, cudaMemcpyDefault);
+        if (e != cudaSuccess) return cuda_fail(e, "read seq_len");
+    }
+    int max_len = 0;
+    for (int b = 0; b < batch; ++b) {
+        if (lens[b] < 0) return fail(LC_ERR_INVALID_ARG, "seq_len[%d] = %d", b, lens[b]);
+        if (lens[b] > max_len) max_len = lens[b];
+    }
+    if (max_len < 1) max_len = 1;
+    // Extent of the K/V buffers in floats.
+    const size_t kv_floats = (size_t)(batch - 1) * seq_stride + (size_t)(n_kv_heads - 1) * head_stride +
+                             (size_t)(max_len - 1) * pos_stride + head_dim;
+    Stager s(c);
+    auto* dq = (const float*)s.arg(q, (size_t)batch * n_heads * head_dim * 4, kIn);
+    auto* dk = (const float*)s.arg(k, kv_floats * 4, kIn);
+    auto* dv = (const float*)s.arg(v, kv_floats * 4, kIn);
+    auto* dout = (float*)s.arg(out, (size_t)batch * n_heads * head_dim * 4, kOut);
+    auto* dl = (const int32_t*)s.arg(lens.data(), (size_t)batch * 4, kIn);
+    if (s.status != LC_OK) return s.status;
+    if (((uintptr_t)dq | (uintptr_t)dk | (uintptr_t)dv) & 15) return fail(LC_ERR_INVALID_ARG, "q/k/v must be 16-byte aligned");
+    AttnPlan plan = plan_attention(batch, n_heads, n_kv_heads, head_dim, max_len, c->sms);
+    const size_t need = attention_scratch_bytes(plan);
+    if (c->attn_scratch_bytes < need) {
+        if (c->attn_scratch) cudaFree(c->attn_scratch);
+        c->attn_scratch = nullptr;
+        c->attn_scratch_bytes = 0;
+        CK(cudaMalloc(&c->attn_scratch, need), "attention scratch");
+        c->attn_scratch_bytes = need;
+    }
+    cudaError_t e = launch_attention_decode(plan, dq, dk, dv, dout, dl, seq_stride, head_stride, pos_stride,
+                                            c->attn_scratch, c->stream);
+    // `lens` is host memory, so the call is staged and finish() synchronises.
+    return s.finish(e);
+}
+
+extern "C" int lc_argmax(lc_context* c, const float* values, int n, int32_t* out_index) {
+    CTX_CHECK(c);
+    if (n <= 0 || !out_index) return fail(LC_ERR_INVALID_ARG, "n=%d out=%p", n, (void*)out_index);
+    Stager s(c);
+    auto* dv = (const float*)s.arg(values, (size_t)n * 4, kIn);
+    auto* di = (int32_t*)s.arg(out_index, 4, kOut);
+    if (s.status != LC_OK) return s.status;
+    launch_argmax(dv, n, di, c->stream);
+    return s.finish(cudaGetLastError());
+}
+
+// -------------------------------------------------------------- model ----
+
+extern "C" void lc_config_llama32_1b(lc_config* o) {
+    if (!o) return;
+    memset(o, 0, sizeof(*o));
+    o->dim = 2048;
+    o->hidden = 8192;
+    o->n_layers = 16;
+    o->n_heads = 32;
+    o->n_kv_heads = 8;
+    o->head_dim = 64;
+    o->vocab = 128256;
+    o->max_seq = 2048;
+    o->rope_theta = 500000.0f;
+    o->rms_eps = 1e-5f;
+}
+
+struct LayerStore {
+    __half *wqkv, *wo, *wgu, *wdown;
+    float *attn_norm, *ffn_norm;
+};
+
+struct lc_model {
+    lc_context* ctx = nullptr;
+    lc_config cfg;
+    void* arena = nullptr;  // all weights, one allocation
+    size_t arena_bytes = 0;
+    __half* tok_emb = nullptr;
+    __half* out_w = nullptr;  // only if "output.weight" is uploaded
+    float* out_norm = nullptr;
+    std::vector<LayerStore> layers;
+    LayerW* d_layers = nullptr;
+    std::vector<uint8_t> have;  // received flags
+    bool has_output = false;
+    bool finalized = false;
+    RopeFreq rope;
+    DecodeLaunch launch;
+};
+
+static int validate_config(const lc_config* c) {
+    if (!c) return fail(LC_ERR_INVALID_ARG, "config is NULL");
+    if (c->dim <= 0 || c->hidden <= 0 || c->n_layers <= 0 || c->n_heads <= 0 || c->n_kv_heads <= 0 ||
+        c->head_dim <= 0 || c->vocab <= 1 || c->max_seq <= 0)
+        return fail(LC_ERR_INVALID_ARG, "config has a non-positive dimension");
+    if (c->n_heads % c->n_kv_heads) return fail(LC_ERR_INVALID_ARG, "n_heads %% n_kv_heads != 0");
+    return LC_OK;
+}
+
+// Tensor slots: 0 tok_emb, 1 output, 2 output_norm, then 9 per layer.
+enum { kTokEmb = 0, kOutput = 1, kOutNorm = 2, kLayerBase = 3 };
+enum { kAttnNorm, kQ, kK, kV, kO, kFfnNorm, kGate, kUp, kDown, kPerLayer };
+
+extern "C" int lc_model_create(lc_context* ctx, const lc_config* cfg, lc_model** out) {
+    CTX_CHECK(ctx);
+    if (!out) return fail(LC_ERR_INVALID_ARG, "out is NULL");
+    int rc = validate_config(cfg);
+    if (rc) return rc;
+    lc_model* m = new lc_model();
+    m->ctx = ctx;
+    m->cfg = *cfg;
+    const lc_config& c = *cfg;
+    const size_t qdim = (size_t)c.n_heads * c.head_dim, kvd = (size_t)c.n_kv_heads * c.head_dim;
+    auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    size_t per_layer = al((qdim + 2 * kvd) * c.dim * 2) + al((size_t)c.dim * qdim * 2) +
+                       al((size_t)2 * c.hidden * c.dim * 2) + al((size_t)c.dim * c.hidden * 2) + 2 * al((size_t)c.dim * 4);
+    size_t total = al((size_t)c.vocab * c.dim * 2) + al((size_t)c.dim * 4) + per_layer * c.n_layers;
+    cudaError_t e = cudaMalloc(&m->arena, total);
+    if (e != cudaSuccess) {
+        delete m;
+        return cuda_fail(e, "weight arena");
+    }
+    m->arena_bytes = total;
+    uint8_t* p = (uint8_t*)m->arena;
+    auto take = [&](size_t b) {
+        uint8_t* r = p;
+        p += al(b);
+        return r;
+    };
+    m->tok_emb = (__half*)take((size_t)c.vocab * c.dim * 2);
+    m->out_norm = (float*)take((size_t)c.dim * 4);
+    m->layers.resize(c.n_layers);
+    for (int l = 0; l < c.n_layers; ++l) {
+        LayerStore& L = m->layers[l];
+        L.wqkv = (__half*)take((qdim + 2 * kvd) * c.dim * 2);
+        L.wo = (__half*)take((size_t)c.dim * qdim * 2);
+        L.wgu = (__half*)take((size_t)2 * c.hidden * c.dim * 2);
+        L.wdown = (__half*)take((size_t)c.dim * c.hidden * 2);
+        L.attn_norm = (float*)take((size_t)c.dim * 4);
+        L.ffn_norm = (float*)take((size_t)c.dim * 4);
+    }
+    m->have.assign(kLayerBase + kPerLayer * c.n_layers, 0);
+    *out = m;
+    return LC_OK;
+}
+
+extern "C" int lc_model_get_config(const lc_model* m, lc_config* out) {
+    if (!m || !out) return fail(LC_ERR_INVALID_ARG, "NULL argument");
+    *out = m->cfg;
+    return LC_OK;
+}
+
+extern "C" int lc_model_destroy(lc_model* m) {
+    if (!m) return LC_OK;
+    cudaSetDevice(m->ctx->device);
+    if (m->arena) cudaFree(m->arena);
+    if (m->out_w) cudaFree(m->out_w);
+    if (m->d_layers) cudaFree(m->d_layers);
+    delete m;
+    return LC_OK;
+}
+
+static float f16_bits_to_float(uint16_t h) {
+    uint32_t sign = ((uint32_t)h & 0x8000u) << 16, e = ((uint32_t)h >> 10) & 0x1fu, mant = (uint32_t)h & 0x3ffu;
+    if (e == 0) {
+        float f = (float)mant * 5.9604644775390625e-8f;
+        return sign ? -f : f;
+    }
+    uint32_t bits = (e == 31) ? (sign | 0x7f800000u | (mant << 13)) : (sign | ((e + 112u) << 23) | (mant << 13));
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+// Copies `bytes` from a host or device source into device memory.
+static int put(void* dst, const void* src, size_t bytes, cudaStream_t st) {
+    CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, st), "tensor upload");
+    return LC_OK;
+}
+
+static int upload_norm(float* dst, const void* data, int64_t n, int dtype, cudaStream_t st) {
+    if (dtype == 0) return put(dst, data, (size_t)n * 4, st);
+    // F16 norm weights are widened like LlamaModel.mapTensor (H/LlamaModel.java:159-164).
+    std::vector<uint16_t> h(n);
+    CK(cudaMemcpy(h.data(), data, (size_t)n * 2, cudaMemcpyDefault), "read F16 norm");
+    std::vector<float> f(n);
+    for (int64_t i = 0; i < n; ++i) f[i] = f16_bits_to_float(h[i]);
+    CK(cudaMemcpyAsync(dst, f.data(), (size_t)n * 4, cudaMemcpyHostToDevice, st), "norm upload");
+    CK(cudaStreamSynchronize(st), "norm upload");
+    return LC_OK;
+}
+
+extern "C" int lc_model_upload_tensor(lc_model* m, const char* name, const void* data, int64_t n, int32_t dtype) {
+    if (!m || !name || !data) return fail(LC_ERR_INVALID_ARG, "NULL argument");
+    CTX_CHECK(m->ctx);
+    if (m->finalized) return fail(LC_ERR_STATE, "model already finalized");
+    if (dtype != 0 && dtype != 1) return fail(LC_ERR_INVALID_ARG, "unsupported tensor type %d for %s (F32=0, F16=1)", dtype, name);
+    const lc_config& c = m->cfg;
+    const int64_t qdim = (int64_t)c.n_heads * c.head_dim, kvd = (int64_t)c.n_kv_heads * c.head_dim;
+    cudaStream_t st = m->ctx->stream;
+    auto expect = [&](int64_t want) -> int {
+        if (n != want)
+            return fail(LC_ERR_SHAPE, "Shape mismatch: tensor %s has %lld elements, expected %lld", name, (long long)n, (long long)want);
+        return LC_OK;
+    };
+    auto need_f16 = [&]() -> int {
+        if (dtype != 1) return fail(LC_ERR_INVALID_ARG, "Expected F16 tensor (type 1), got type %d for tensor: %s", dtype, name);
+        return LC_OK;
+    };
+    int rc;
+    if (!strcmp(name, "token_embd.weight") || !strcmp(name, "output.weight")) {
+        if ((rc = need_f16()) || (rc = expect((int64_t)c.vocab * c.dim))) return rc;
+        const bool out_w = name[0] == 'o';
+        __half* dst = m->tok_emb;
+        if (out_w) {
+            if (!m->out_w) CK(cudaMalloc(&m->out_w, (size_t)c.vocab * c.dim * 2), "output.weight");
+            dst = m->out_w;
+        }
+        if ((rc = put(dst, data, (size_t)n * 2, st))) return rc;
+        m->have[out_w ? kOutput : kTokEmb] = 1;
+        m->has_output |= out_w;
+    } else if (!strcmp(name, "output_norm.weight")) {
+        if ((rc = expect(c.dim)) || (rc = upload_norm(m->out_norm, data, n, dtype, st))) return rc;
+        m->have[kOutNorm] = 1;
+    } else if (!strncmp(name, "blk.", 4)) {
+        char* end = nullptr;
+        long l = strtol(name + 4, &end, 10);
+        if (end == name + 4 || *end != '.' || l < 0 || l >= c.n_layers)
+            return fail(LC_ERR_NOT_FOUND, "Tensor not found: %s", name);
+        const char* t = end + 1;
+        LayerStore& L = m->layers[l];
+        int slot;
+        if (!strcmp(t, "attn_norm.weight")) {
+            if ((rc = expect(c.dim)) || (rc = upload_norm(L.attn_norm, data, n, dtype, st))) return rc;
+            slot = kAttnNorm;
+        } else if (!strcmp(t, "ffn_norm.weight")) {
+            if ((rc = expect(c.dim)) || (rc = upload_norm(L.ffn_norm, data, n, dtype, st))) return rc;
+            slot = kFfnNorm;
+        } else if (!strcmp(t, "attn_q.weight") || !strcmp(t, "attn_k.weight") || !strcmp(t, "attn_v.weight")) {
+            const int64_t rows = (t[5] == 'q') ? qdim : kvd;
+            if ((rc = need_f16()) || (rc = expect(rows * c.dim))) return rc;
+            const int64_t row0 = (t[5] == 'q') ? 0 : (t[5] == 'k') ? qdim : qdim + kvd;
+            if ((rc = put(L.wqkv + row0 * c.dim, data, (size_t)n * 2, st))) return rc;
+            slot = (t[5] == 'q') ? kQ : (t[5] == 'k') ? kK : kV;
+        } else if (!strcmp(t, "attn_output.weight")) {
+            if ((rc = need_f16()) || (rc = expect((int64_t)c.dim * qdim))) return rc;
+            if ((rc = put(L.wo, data, (size_t)n * 2, st))) return rc;
+            slot = kO;
+        } else if (!strcmp(t, "ffn_gate.weight") || !strcmp(t, "ffn_up.weight")) {
+            if ((rc = need_f16()) || (rc = expect((int64_t)c.hidden * c.dim))) return rc;
+            // Row r of gate -> row 2r of the packed matrix, row r of up -> 2r+1.
+            const bool up = t[4] == 'u';
+            const size_t rowb = (size_t)c.dim * 2;
+            CK(cudaMemcpy2DAsync((uint8_t*)L.wgu + (up ? rowb : 0), 2 * rowb, data, rowb, rowb, (size_t)c.hidden,
+                                 cudaMemcpyDefault, st),
+               "gate/up upload");
+            slot = up ? kUp : kGate;
+        } else if (!strcmp(t, "ffn_down.weight")) {
+            if ((rc = need_f16()) || (rc = expect((int64_t)c.dim * c.hidden))) return rc;
+            if ((rc = put(L.wdown, data, (size_t)n * 2, st))) return rc;
+            slot = kDown;
+        } else {
+            return fail(LC_ERR_NOT_FOUND, "Tensor not found: %s", name);
+        }
+        m->have[kLayerBase + kPerLayer * l + slot] = 1;
+    } else {
+        return fail(LC_ERR_NOT_FOUND, "Tensor not found: %s", name);
+    }
+    // Host sources may be freed once the call returns.
+    CK(cudaStreamSynchronize(st), "tensor upload");
+    return LC_OK;
+}
+
+static const char* slot_name(int slot, char* buf) {
+    static const char* per[] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_output",
+                                "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"};
+    if (slot == kTokEmb) return "token_embd.weight";
+    if (slot == kOutNorm) return "output_norm.weight";
+    int l = (slot - kLayerBase) / kPerLayer, k = (slot - kLayerBase) % kPerLayer;
+    snprintf(buf, 64, "blk.%d.%s.weight", l, per[k]);
+    return buf;
+}
+
+static void fill_model_params(const lc_model* m, DecodeParams* p) {
+    const lc_config& c = m->cfg;
+    memset(p, 0, sizeof(*p));
+    p->dim = c.dim;
+    p->hidden = c.hidden;
+    p->n_layers = c.n_layers;
+    p->n_heads = c.n_heads;
+    p->n_kv = c.n_kv_heads;
+    p->head_dim = c.head_dim;
+    p->vocab = c.vocab;
+    p->max_seq = c.max_seq;
+    p->eps = c.rms_eps;
+    p->attn_scale = 1.0f / (float)sqrt((double)c.head_dim);  // Attention.java:33
+    p->tok_emb = m->tok_emb;
+    p->lm_head = m->has_output ? m->out_w : m->tok_emb;      // tied, LlamaInference.java:69-72
+    p->out_norm = m->out_norm;
+    p->layers = m->d_layers;
+    p->rope = m->rope;
+    p->timeout_ns = 2000000000ull;
+}
+
+extern "C" int lc_model_finalize(lc_model* m) {
+    if (!m) return fail(LC_ERR_INVALID_ARG, "model is NULL");
+    CTX_CHECK(m->ctx);
+    if (m->finalized) return LC_OK;
+    char buf[64];
+    for (size_t s = 0; s < m->have.size(); ++s) {
+        if (s == kOutput) continue;  // optional: tied embeddings
+        if (!m->have[s]) return fail(LC_ERR_NOT_FOUND, "Tensor not found: %s", slot_name((int)s, buf));
+    }
+    make_rope_freq(&m->rope, m->cfg.rope_theta, m->cfg.head_dim);
+    std::vector<LayerW> lw(m->cfg.n_layers);
+    for (int l = 0; l < m->cfg.n_layers; ++l) {
+        const LayerStore& L = m->layers[l];
+        lw[l] = {L.wqkv, L.wo, L.wgu, L.wdown, L.attn_norm, L.ffn_norm};
+    }
+    CK(cudaMalloc(&m->d_layers, lw.size() * sizeof(LayerW)), "layer table");
+    CK(cudaMemcpy(m->d_layers, lw.data(), lw.size() * sizeof(LayerW), cudaMemcpyHostToDevice), "layer table");
+    DecodeParams p;
+    fill_model_params(m, &p);
+    const char* why = nullptr;
+    if (!decode_plan(p, m->ctx->sms, &m->launch, &why)) return fail(LC_ERR_UNSUPPORTED, "%s", why);
+    CK(decode_prepare(m->launch), "decode kernel setup");
+    m->finalized = true;
+    return LC_OK;
+}
+
+// ------------------------------------------------------------ session ----
+
+struct lc_session {
+    lc_model* m = nullptr;
+    void* mem = nullptr;
+    float *kcache, *vcache, *x, *qbuf, *att, *hbuf, *logits, *attn_part, *amax_val;
+    uint32_t *attn_cnt, *bar;
+    int *amax_idx, *err, *n_done;
+    int32_t* tokens;
+    int attn_max_splits = 0;
+    int32_t* pinned = nullptr;  // host staging for small transfers
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    float last_ms = 0.0f;
+};
+
+extern "C" int lc_session_create(lc_model* m, lc_session** out) {
+    if (!m || !out) return fail(LC_ERR_INVALID_ARG, "NULL argument");
+    CTX_CHECK(m->ctx);
+    if (!m->finalized) return fail(LC_ERR_STATE, "model not finalized");
+    const lc_config& c = m->cfg;
+    lc_session* s = new lc_session();
+    s->m = m;
+    const int kv_mul = c.n_heads / c.n_kv_heads;
+    s->attn_max_splits = (c.max_seq + 63) / 64;
+    const size_t G = (size_t)m->launch.grid;
+    auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t kv = (size_t)c.n_layers * c.n_kv_heads * c.max_seq * c.head_dim * 4;
+    const size_t qd = (size_t)c.n_heads * c.head_dim * 4;
+    size_t sizes[] = {kv, kv, (size_t)c.dim * 4, qd, qd, (size_t)c.hidden * 4, (size_t)c.vocab * 4,
+                      (size_t)c.n_kv_heads * s->attn_max_splits * kv_mul * kAttnPartStride * 4, G * 4,
+                      (size_t)c.n_kv_heads * 4, 4, G * 4, 4, 4, (size_t)(c.max_seq + 1) * 4};
+    size_t total = 0;
+    for (size_t b : sizes) total += al(b);
+    cudaError_t e = cudaMalloc(&s->mem, total);
+    if (e != cudaSuccess) {
+        delete s;
+        return cuda_fail(e, "session buffers");
+    }
+    uint8_t* p = (uint8_t*)s->mem;
+    void* ptrs[15];
+    for (int i = 0; i < 15; ++i) {
+        ptrs[i] = p;
+        p += al(sizes[i]);
+    }
+    s->kcache = (float*)ptrs[0];
+    s->vcache = (float*)ptrs[1];
+    s->x = (float*)ptrs[2];
+    s->qbuf = (float*)ptrs[3];
+    s->att = (float*)ptrs[4];
+    s->hbuf = (float*)ptrs[5];
+    s->logits = (float*)ptrs[6];
+    s->attn_part = (float*)ptrs[7];
+    s->amax_val = (float*)ptrs[8];
+    s->attn_cnt = (uint32_t*)ptrs[9];
+    s->bar = (uint32_t*)ptrs[10];
+    s->amax_idx = (int*)ptrs[11];
+    s->err = (int*)ptrs[12];
+    s->n_done = (int*)ptrs[13];
+    s->tokens = (int32_t*)ptrs[14];
+    e = cudaMemset(s->mem, 0, total);
+    if (e == cudaSuccess) e = cudaMallocHost((void**)&s->pinned, (size_t)(c.max_seq + 8) * 4);
+    if (e == cudaSuccess) e = cudaEventCreate(&s->ev0);
+    if (e == cudaSuccess) e = cudaEventCreate(&s->ev1);
+    if (e != cudaSuccess) {
+        lc_session_destroy(s);
+        return cuda_fail(e, "session setup");
+    }
+    *out = s;
+    return LC_OK;
+}
+
+extern "C" int lc_session_destroy(lc_session* s) {
+    if (!s) return LC_OK;
+    cudaSetDevice(s->m->ctx->device);
+    cudaStreamSynchronize(s->m->ctx->stream);
+    if (s->mem) cudaFree(s->mem);
+    if (s->pinned) cudaFreeHost(s->pinned);
+    if (s->ev0) cudaEventDestroy(s->ev0);
+    if (s->ev1) cudaEventDestroy(s->ev1);
+    delete s;
+    return LC_OK;
+}
+
+// Launches the fused kernel for positions pos0..pos0+nsteps-1 and waits.
+static int run_steps(lc_session* s, int pos0, int nsteps, int n_prompt, int skip_prefill_logits,
+                     const int32_t* stop, int n_stop, int* n_done) {
+    lc_model* m = s->m;
+    cudaStream_t st = m->ctx->stream;
+    DecodeParams p;
+    fill_model_params(m, &p);
+    p.kcache = s->kcache;
+    p.vcache = s->vcache;
+    p.x = s->x;
+    p.qbuf = s->qbuf;
+    p.att = s->att;
+    p.hbuf = s->hbuf;
+    p.logits = s->logits;
+    p.attn_part = s->attn_part;
+    p.attn_cnt = s->attn_cnt;
+    p.amax_val = s->amax_val;
+    p.amax_idx = s->amax_idx;
+    p.tokens = s->tokens;
+    p.bar = s->bar;
+    p.err = s->err;
+    p.n_done = s->n_done;
+    p.pos0 = pos0;
+    p.nsteps = nsteps;
+    p.n_prompt = n_prompt;
+    p.skip_prefill_logits = skip_prefill_logits;
+    p.n_stop = n_stop;
+    for (int i = 0; i < n_stop; ++i) p.stop[i] = stop[i];
+    p.attn_max_splits = s->attn_max_splits;
+    CK(cudaMemsetAsync(s->err, 0, sizeof(int), st), "clear error word");
+    CK(cudaMemsetAsync(s->attn_cnt, 0, (size_t)m->cfg.n_kv_heads * 4, st), "clear attention counters");
+    CK(cudaEventRecord(s->ev0, st), "event");
+    CK(launch_decode(p, m->launch, st), "decode kernel launch");
+    CK(cudaEventRecord(s->ev1, st), "event");
+    CK(cudaMemcpyAsync(s->pinned, s->err, 4, cudaMemcpyDeviceToHost, st), "read error word");
+    CK(cudaMemcpyAsync(s->pinned + 1, s->n_done, 4, cudaMemcpyDeviceToHost, st), "read step count");
+    CK(cudaStreamSynchronize(st), "decode kernel");
+    cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1);
+    const int err = s->pinned[0];
+    if (err != 0) {
+        if (err == kDevBadToken) return fail(LC_ERR_INVALID_ARG, "token id outside [0, %d)", m->cfg.vocab);
+        return fail(LC_ERR_TIMEOUT, "decode kernel: bounded device wait gave up (code %d)", err);
+    }
+    *n_done = s->pinned[1];
+    return LC_OK;
+}
+
+extern "C" int lc_forward(lc_session* s, int32_t token, int32_t pos, float* logits, int32_t* argmax_out) {
+    if (!s) return fail(LC_ERR_INVALID_ARG, "session is NULL");
+    CTX_CHECK(s->m->ctx);
+    const lc_config& c = s->m->cfg;
+    if (token < 0 || token >= c.vocab) return fail(LC_ERR_INVALID_ARG, "token %d outside [0, %d)", token, c.vocab);
+    if (pos < 0 || pos >= c.max_seq) return fail(LC_ERR_INVALID_ARG, "pos %d outside [0, %d)", pos, c.max_seq);
+    cudaStream_t st = s->m->ctx->stream;
+    s->pinned[2] = token;
+    CK(cudaMemcpyAsync(s->tokens + pos, s->pinned + 2, 4, cudaMemcpyHostToDevice, st), "token upload");
+    int done = 0;
+    int rc = run_steps(s, pos, 1, 0, 0, nullptr, 0, &done);
+    if (rc) return rc;
+    if (logits) CK(cudaMemcpyAsync(logits, s->logits, (size_t)c.vocab * 4, cudaMemcpyDefault, st), "logits copy");
+    if (argmax_out) CK(cudaMemcpyAsync(argmax_out, s->tokens + pos + 1, 4, cudaMemcpyDefault, st), "argmax copy");
+    CK(cudaStreamSynchronize(st), "forward");
+    return LC_OK;
+}
+
+extern "C" int lc_generate(lc_session* s, const int32_t* prompt, int32_t n_prompt, int32_t max_new,
+                           const int32_t* stop, int32_t n_stop, int32_t* out_tokens, int32_t* n_out) {
+    if (!s || !prompt || !out_tokens || !n_out) return fail(LC_ERR_INVALID_ARG, "NULL argument");
+    CTX_CHECK(s->m->ctx);
+    const lc_config& c = s->m->cfg;
+    if (n_prompt <= 0) return fail(LC_ERR_INVALID_ARG, "empty prompt");
+    if (max_new <= 0) return fail(LC_ERR_INVALID_ARG, "max_new must be positive");
+    if ((int64_t)n_prompt + max_new - 1 > c.max_seq)
+        return fail(LC_ERR_INVALID_ARG, "prompt %d + %d new tokens exceed max_seq %d", n_prompt, max_new, c.max_seq);
+    if (n_stop < 0 || n_stop > kMaxStop || (n_stop > 0 && !stop))
+        return fail(LC_ERR_UNSUPPORTED, "n_stop=%d (at most %d stop tokens)", n_stop, kMaxStop);
+    cudaStream_t st = s->m->ctx->stream;
+    int32_t hstop[kMaxStop];
+    if (n_stop) CK(cudaMemcpy(hstop, stop, (size_t)n_stop * 4, cudaMemcpyDefault), "stop tokens");
+    CK(cudaMemcpyAsync(s->tokens, prompt, (size_t)n_prompt * 4, cudaMemcpyDefault, st), "prompt upload");
+    int done = 0;
+    int rc = run_steps(s, 0, n_prompt + max_new - 1, n_prompt, 1, hstop, n_stop, &done);
+    if (rc) return rc;
+    const int n_gen = done - (n_prompt - 1);
+    if (n_gen > 0)
+        CK(cudaMemcpyAsync(out_tokens, s->tokens + n_prompt, (size_t)n_gen * 4, cudaMemcpyDefault, st), "tokens copy");
+    CK(cudaStreamSynchronize(st), "generate");
+    *n_out = n_gen > 0 ? n_gen : 0;
+    return LC_OK;
+}
+
+extern "C" int lc_decode(lc_session* s, int32_t token, int32_t start_pos, int32_t n_steps, int32_t* out_tokens) {
+    if (!s || !out_tokens) return fail(LC_ERR_INVALID_ARG, "NULL argument");
+    CTX_CHECK(s->m->ctx);
+    const lc_config& c = s->m->cfg;
+    if (token < 0 || token >= c.vocab) return fail(LC_ERR_INVALID_ARG, "token %d outside [0, %d)", token, c.vocab);
+    if (n_steps <= 0 || start_pos < 0 || (int64_t)start_pos + n_steps > c.max_seq)
+        return fail(LC_ERR_INVALID_ARG, "start_pos=%d n_steps=%d max_seq=%d", start_pos, n_steps, c.max_seq);
+    cudaStream_t st = s->m->ctx->stream;
+    s->pinned[2] = token;
+    CK(cudaMemcpyAsync(s->tokens + start_pos, s->pinned + 2, 4, cudaMemcpyHostToDevice, st), "token upload");
+    int done = 0;
+    int rc = run_steps(s, start_pos, n_steps, 0, 0, nullptr, 0, &done);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(out_tokens, s->tokens + start_pos + 1, (size_t)n_steps * 4, cudaMemcpyDefault, st), "tokens copy");
+    CK(cudaStreamSynchronize(st), "decode");
+    return LC_OK;
+}
+
+extern "C" int lc_session_last_ms(lc_session* s, float* ms) {
+    if (!s || !ms) return fail(LC_ERR_INVALID_ARG, "NULL argument");
+    *ms = s->last_ms;
+    return LC_OK;
+}
+
+// Error hook for lc_gguf.cpp (not part of the public ABI).
+extern "C" __attribute__((visibility("hidden"))) int lc_gguf_set_error(int code, const char* msg) {
+    return fail(code, "%s", msg);
+}

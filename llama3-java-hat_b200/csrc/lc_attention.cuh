@@ -1,0 +1,143 @@
+// lc_attention.cuh -- one unit of GQA split-KV decode attention.
+//
+// A unit is (sequence, kv head, split of positions [t0, t1)).  It serves the
+// kv_mul = n_heads / n_kv query heads that share the kv head (GQA, 4:1 for
+// Llama-3.2-1B; TransformerBlock.java:165-168).  256 threads cooperate through
+// named barrier 1 (the consumer warps of the fused decode kernel, or the whole
+// CTA of the standalone launch).
+//
+// With a single split the unit reproduces the reference loop order exactly:
+// sequential score dot products (Attention.java:36-40), max, exp in double,
+// sequential sum, p = e * (1/sum) (Softmax.java:30-50), sequential weighted
+// values (Attention.java:54-60) -- bit-identical to the Java kernels for the
+// same q, K and V.  With several splits each unit writes a partial
+// (max, sum, unnormalised output) and the last unit to finish (ticket on a
+// completion counter) merges them (flash-decoding combine).
+#pragma once
+
+#include "lc_common.cuh"
+
+namespace lc {
+
+constexpr int kAttnHeadDim = 64;
+
+// Shared-memory floats a unit needs.
+__host__ __device__ inline int attn_unit_smem_floats(int kv_mul, int tmax) {
+    return kv_mul * kAttnHeadDim + kv_mul * tmax + 2 * kv_mul + 4;
+}
+
+// Partial record per (split, head): [m, l, o[64]].
+constexpr int kAttnPartStride = kAttnHeadDim + 2;
+
+__device__ __forceinline__ void attention_unit(const float* __restrict__ q, const float* __restrict__ K,
+                                               const float* __restrict__ Vc, int64_t pos_stride, int t0, int t1,
+                                               int nsplit, int split, float* __restrict__ out,
+                                               float* __restrict__ part, uint32_t* cnt, float scale, int kv_mul,
+                                               int tmax, float* sm) {
+    constexpr int HD = kAttnHeadDim;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int T = t1 - t0;
+    float* qs = sm;
+    float* sc = qs + kv_mul * HD;
+    float* st = sc + kv_mul * tmax;
+    volatile int* flag = reinterpret_cast<volatile int*>(st + 2 * kv_mul);
+
+    for (int i = tid; i < kv_mul * HD; i += 256) qs[i] = __ldcg(q + i);
+    named_bar_sync(1, 256);
+
+    // Scores: consecutive threads take the kv_mul heads of one position.
+    for (int idx = tid; idx < T * kv_mul; idx += 256) {
+        const int h = idx % kv_mul, tt = idx / kv_mul;
+        const float4* kr = reinterpret_cast<const float4*>(K + (int64_t)(t0 + tt) * pos_stride);
+        const float* qh = qs + h * HD;
+        float sum = 0.0f;
+#pragma unroll
+        for (int c = 0; c < HD / 4; ++c) {
+            const float4 k4 = __ldcg(kr + c);
+            sum = __fadd_rn(sum, __fmul_rn(qh[4 * c + 0], k4.x));
+            sum = __fadd_rn(sum, __fmul_rn(qh[4 * c + 1], k4.y));
+            sum = __fadd_rn(sum, __fmul_rn(qh[4 * c + 2], k4.z));
+            sum = __fadd_rn(sum, __fmul_rn(qh[4 * c + 3], k4.w));
+        }
+        sc[h * tmax + tt] = __fmul_rn(sum, scale);
+    }
+    named_bar_sync(1, 256);
+
+    // Per head: max, e = exp(s - max), sum.
+    for (int h = warp; h < kv_mul; h += 8) {
+        float* e = sc + h * tmax;
+        float m = -INFINITY;
+        for (int t = lane; t < T; t += 32) m = fmaxf(m, e[t]);
+        m = warp_max(m);
+        for (int t = lane; t < T; t += 32) e[t] = exp_via_double(__fsub_rn(e[t], m));
+        __syncwarp();
+        float l = 0.0f;
+        if (nsplit == 1) {
+            if (lane == 0)
+                for (int t = 0; t < T; ++t) l = __fadd_rn(l, e[t]);
+            l = __shfl_sync(0xffffffffu, l, 0);
+        } else {
+            for (int t = lane; t < T; t += 32) l += e[t];
+            l = warp_sum(l);
+        }
+        if (lane == 0) {
+            st[2 * h] = m;
+            st[2 * h + 1] = l;
+        }
+    }
+    named_bar_sync(1, 256);
+
+    // Weighted values: thread per (head, dim), sequential over positions.
+    for (int hi = tid; hi < kv_mul * HD; hi += 256) {
+        const int h = hi / HD, i = hi % HD;
+        const float* e = sc + h * tmax;
+        const float* vcol = Vc + (int64_t)t0 * pos_stride + i;
+        float acc = 0.0f;
+        if (nsplit == 1) {
+            const float inv = __fdiv_rn(1.0f, st[2 * h + 1]);
+#pragma unroll 4
+            for (int t = 0; t < T; ++t)
+                acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(e[t], inv), __ldcg(vcol + (int64_t)t * pos_stride)));
+            out[h * HD + i] = acc;
+        } else {
+#pragma unroll 4
+            for (int t = 0; t < T; ++t) acc = fmaf(e[t], __ldcg(vcol + (int64_t)t * pos_stride), acc);
+            float* pp = part + ((int64_t)split * kv_mul + h) * kAttnPartStride;
+            pp[2 + i] = acc;
+            if (i == 0) {
+                pp[0] = st[2 * h];
+                pp[1] = st[2 * h + 1];
+            }
+        }
+    }
+
+    if (nsplit > 1) {
+        __threadfence();
+        named_bar_sync(1, 256);
+        if (tid == 0) {
+            const uint32_t ticket = atomicAdd(cnt, 1u);
+            *flag = (ticket == (uint32_t)(nsplit - 1)) ? 1 : 0;
+        }
+        named_bar_sync(1, 256);
+        if (*flag) {
+            __threadfence();
+            for (int hi = tid; hi < kv_mul * HD; hi += 256) {
+                const int h = hi / HD, i = hi % HD;
+                float M = -INFINITY;
+                for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(part + ((int64_t)s * kv_mul + h) * kAttnPartStride));
+                float L = 0.0f, O = 0.0f;
+                for (int s = 0; s < nsplit; ++s) {
+                    const float* pp = part + ((int64_t)s * kv_mul + h) * kAttnPartStride;
+                    const float w = exp_via_double(__fsub_rn(__ldcg(pp), M));
+                    L = fmaf(__ldcg(pp + 1), w, L);
+                    O = fmaf(__ldcg(pp + 2 + i), w, O);
+                }
+                out[h * HD + i] = __fdiv_rn(O, L);
+            }
+            if (tid == 0) atomicExch(cnt, 0u);
+        }
+    }
+    named_bar_sync(1, 256);
+}
+
+}  // namespace lc

@@ -1,0 +1,395 @@
+// lc_kernels.cu -- standalone sm_100a kernels behind the per-kernel operators
+// of the C ABI (the IKernelFactory surface): generic GEMV, RMSNorm, RoPE,
+// SiLU / SwiGLU, softmax, attention scores/values, fused GQA split-KV decode
+// attention and argmax.
+//
+// Numerics follow the reference's plain-Java kernels: binary32 arithmetic,
+// exp/sin/cos evaluated in double and rounded to float where the Java code
+// writes (float)Math.*, explicit round-to-nearest intrinsics (__fmul_rn /
+// __fadd_rn) where the Java expression order must not be contracted into an
+// FMA.  Reductions run as trees where the reference is sequential; that order
+// difference is the only deviation.
+#include "lc_internal.h"
+
+namespace lc {
+
+// ------------------------------------------------------------------ GEMV --
+
+// Warp per row, any shape and alignment.  Lane-strided fp32 partial sums then
+// a shuffle tree.  Used for shapes the streaming GEMV does not take.
+template <typename WT>
+__global__ void gemv_generic_kernel(const WT* __restrict__ W, const float* __restrict__ x, float* __restrict__ y,
+                                    int rows, int cols) {
+    const int lane = threadIdx.x & 31;
+    const int warps = (gridDim.x * blockDim.x) >> 5;
+    for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows; r += warps) {
+        const WT* w = W + (size_t)r * (size_t)cols;
+        float acc = 0.0f;
+        for (int c = lane; c < cols; c += 32) {
+            float wv;
+            if constexpr (sizeof(WT) == 2) wv = __half2float(__ushort_as_half(w[c]));
+            else wv = w[c];
+            acc = fmaf(wv, x[c], acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) y[r] = acc;
+    }
+}
+
+void launch_gemv_generic_f16(const uint16_t* W, const float* x, float* y, int rows, int cols, cudaStream_t st) {
+    int blocks = (rows + 7) / 8;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    gemv_generic_kernel<uint16_t><<<blocks, 256, 0, st>>>(W, x, y, rows, cols);
+}
+
+void launch_gemv_generic_f32(const float* W, const float* x, float* y, int rows, int cols, cudaStream_t st) {
+    int blocks = (rows + 7) / 8;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    gemv_generic_kernel<float><<<blocks, 256, 0, st>>>(W, x, y, rows, cols);
+}
+
+// Batched F16 GEMV on CUDA cores: one warp per (row, group of up to 8
+// sequences).  X rows are read through L1; W row re-read once per group.
+__global__ void gemv_batched_kernel(const uint16_t* __restrict__ W, const float* __restrict__ X, float* __restrict__ Y,
+                                    int rows, int cols, int batch) {
+    const int lane = threadIdx.x & 31;
+    const int groups = (batch + 7) / 8;
+    const long long total = (long long)rows * groups;
+    const long long warps = ((long long)gridDim.x * blockDim.x) >> 5;
+    for (long long t = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < total; t += warps) {
+        const int r = (int)(t / groups);
+        const int b0 = (int)(t % groups) * 8;
+        const int nb = min(8, batch - b0);
+        const uint16_t* w = W + (size_t)r * (size_t)cols;
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+        for (int c = lane; c < cols; c += 32) {
+            float wv = __half2float(__ushort_as_half(w[c]));
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (j < nb) acc[j] = fmaf(wv, X[(size_t)(b0 + j) * cols + c], acc[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float s = warp_sum(acc[j]);
+            if (lane == 0 && j < nb) Y[(size_t)(b0 + j) * rows + r] = s;
+        }
+    }
+}
+
+void launch_gemv_batched_f16(const uint16_t* W, const float* X, float* Y, int rows, int cols, int batch,
+                             cudaStream_t st) {
+    long long work = (long long)rows * ((batch + 7) / 8);
+    long long blocks = (work + 7) / 8;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    gemv_batched_kernel<<<(int)blocks, 256, 0, st>>>(W, X, Y, rows, cols, batch);
+}
+
+// --------------------------------------------------------------- RMSNorm --
+
+template <int NT>
+LC_DEV float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    float s = 0.0f;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NT / 32; ++i) s += red[i];
+        red[32] = s;
+    }
+    __syncthreads();
+    s = red[32];
+    __syncthreads();
+    return s;
+}
+
+// One CTA per row: sum of squares (tree), invRms exactly as RMSNorm.java:43,
+// then x*invRms*w left to right (RMSNorm.java:48).  In place.
+__global__ void rmsnorm_rows_kernel(float* __restrict__ x, const float* __restrict__ w, int width, float eps) {
+    __shared__ float red[33];
+    float* row = x + (size_t)blockIdx.x * (size_t)width;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < width; i += 256) {
+        float v = row[i];
+        ss = fmaf(v, v, ss);
+    }
+    ss = block_sum<256>(ss, red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)width), eps)));
+    for (int i = threadIdx.x; i < width; i += 256) row[i] = __fmul_rn(__fmul_rn(row[i], inv), w[i]);
+}
+
+void launch_rmsnorm_rows(float* x, const float* w, int rows, int width, float eps, cudaStream_t st) {
+    rmsnorm_rows_kernel<<<rows, 256, 0, st>>>(x, w, width, eps);
+}
+
+// ------------------------------------------------------------------ RoPE --
+
+// Thread per (row, head, pair).  freq[] is computed on the host in double
+// exactly like RoPE.java:42; the angle is a float product (RoPE.java:43) and
+// cos/sin are evaluated in double then rounded (RoPE.java:44-45).
+__global__ void rope_rows_kernel(float* __restrict__ vec, const int32_t* __restrict__ pos, int rows, int num_heads,
+                                 int head_dim, RopeFreq fq) {
+    const int half = head_dim >> 1;
+    const long long pairs_per_row = (long long)num_heads * half;
+    const long long total = pairs_per_row * rows;
+    for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(t / pairs_per_row);
+        const int rem = (int)(t % pairs_per_row);
+        const int h = rem / half, j = rem % half;
+        float* v = vec + (size_t)r * num_heads * head_dim + (size_t)h * head_dim + 2 * j;
+        const float val = __fmul_rn((float)pos[r], fq.f[j]);
+        double s, c;
+        sincos((double)val, &s, &c);
+        const float cf = (float)c, sf = (float)s;
+        const float v0 = v[0], v1 = v[1];
+        v[0] = __fsub_rn(__fmul_rn(v0, cf), __fmul_rn(v1, sf));
+        v[1] = __fadd_rn(__fmul_rn(v0, sf), __fmul_rn(v1, cf));
+    }
+}
+
+void launch_rope_rows(float* vec, const int32_t* pos, int rows, int num_heads, int head_dim, const RopeFreq& fq,
+                      cudaStream_t st) {
+    long long total = (long long)rows * num_heads * (head_dim / 2);
+    long long blocks = (total + 255) / 256;
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    if (blocks < 1) blocks = 1;
+    rope_rows_kernel<<<(int)blocks, 256, 0, st>>>(vec, pos, rows, num_heads, head_dim, fq);
+}
+
+// ----------------------------------------------------------- SiLU/SwiGLU --
+
+__global__ void silu_kernel(float* __restrict__ x, long long n) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        x[i] = silu_ref(x[i]);
+}
+
+// g = silu(g) * u : SiLU.java:36-39 then TransformerBlock.elementWiseMul.
+__global__ void swiglu_kernel(float* __restrict__ g, const float* __restrict__ u, long long n) {
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool vec4 = ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(u)) & 15) == 0;
+    if (vec4) {
+        const long long n4 = n >> 2;
+        for (long long k = i; k < n4; k += stride) {
+            float4 a = reinterpret_cast<float4*>(g)[k];
+            const float4 b = __ldg(reinterpret_cast<const float4*>(u) + k);
+            a.x = __fmul_rn(silu_ref(a.x), b.x);
+            a.y = __fmul_rn(silu_ref(a.y), b.y);
+            a.z = __fmul_rn(silu_ref(a.z), b.z);
+            a.w = __fmul_rn(silu_ref(a.w), b.w);
+            reinterpret_cast<float4*>(g)[k] = a;
+        }
+        for (long long k = (n4 << 2) + i; k < n; k += stride) g[k] = __fmul_rn(silu_ref(g[k]), u[k]);
+    } else {
+        for (; i < n; i += stride) g[i] = __fmul_rn(silu_ref(g[i]), u[i]);
+    }
+}
+
+static int ew_blocks(long long n) {
+    long long b = (n + 1023) / 1024;
+    if (b > 148 * 8) b = 148 * 8;
+    return b < 1 ? 1 : (int)b;
+}
+
+void launch_silu(float* x, long long n, cudaStream_t st) { silu_kernel<<<ew_blocks(n), 256, 0, st>>>(x, n); }
+
+void launch_swiglu(float* g, const float* u, long long n, cudaStream_t st) {
+    swiglu_kernel<<<ew_blocks(n), 256, 0, st>>>(g, u, n);
+}
+
+// --------------------------------------------------------------- Softmax --
+
+// Online softmax statistics: merge (m, l) pairs, l relative to m.
+LC_DEV void online_merge(float& m, float& l, float m2, float l2) {
+    if (m2 == -INFINITY) return;
+    if (m == -INFINITY) {
+        m = m2;
+        l = l2;
+        return;
+    }
+    if (m2 > m) {
+        l = fmaf(l, exp_via_double(m - m2), l2);
+        m = m2;
+    } else {
+        l = fmaf(l2, exp_via_double(m2 - m), l);
+    }
+}
+
+// One CTA per row, the row held in registers: one read pass computes the
+// online (max, sum) statistics, one write pass emits exp(x-max) * (1/sum) --
+// the output values use the exact reference expressions (Softmax.java:41,47-49)
+// with the global max; only the accumulation order of the sum differs.
+template <int EPT>
+__global__ void softmax_rows_kernel(float* __restrict__ x, int width) {
+    __shared__ float sm[32], sl[32];
+    float* row = x + (size_t)blockIdx.x * (size_t)width;
+    float v[EPT];
+    float m = -INFINITY, l = 0.0f;
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+        const int i = threadIdx.x + k * 256;
+        v[k] = (i < width) ? row[i] : -INFINITY;
+        if (i < width) {
+            if (v[k] > m) {
+                l = (m == -INFINITY) ? 0.0f : l * exp_via_double(m - v[k]);
+                m = v[k];
+            }
+            l += exp_via_double(v[k] - m);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        float l2 = __shfl_xor_sync(0xffffffffu, l, o);
+        online_merge(m, l, m2, l2);
+    }
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sm[w] = m;
+        sl[w] = l;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float M = sm[0], L = sl[0];
+        for (int i = 1; i < 8; ++i) online_merge(M, L, sm[i], sl[i]);
+        sm[0] = M;
+        sl[0] = L;
+    }
+    __syncthreads();
+    const float M = sm[0];
+    const float inv = __fdiv_rn(1.0f, sl[0]);
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+        const int i = threadIdx.x + k * 256;
+        if (i < width) row[i] = __fmul_rn(exp_via_double(__fsub_rn(v[k], M)), inv);
+    }
+}
+
+// Rows wider than the register budget: same statistics, row re-read.
+__global__ void softmax_rows_wide_kernel(float* __restrict__ x, int width) {
+    __shared__ float sm[32], sl[32];
+    float* row = x + (size_t)blockIdx.x * (size_t)width;
+    float m = -INFINITY, l = 0.0f;
+    for (int i = threadIdx.x; i < width; i += 256) {
+        const float v = row[i];
+        if (v > m) {
+            l = (m == -INFINITY) ? 0.0f : l * exp_via_double(m - v);
+            m = v;
+        }
+        l += exp_via_double(v - m);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+        float l2 = __shfl_xor_sync(0xffffffffu, l, o);
+        online_merge(m, l, m2, l2);
+    }
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sm[w] = m;
+        sl[w] = l;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float M = sm[0], L = sl[0];
+        for (int i = 1; i < 8; ++i) online_merge(M, L, sm[i], sl[i]);
+        sm[0] = M;
+        sl[0] = L;
+    }
+    __syncthreads();
+    const float M = sm[0];
+    const float inv = __fdiv_rn(1.0f, sl[0]);
+    for (int i = threadIdx.x; i < width; i += 256) row[i] = __fmul_rn(exp_via_double(__fsub_rn(row[i], M)), inv);
+}
+
+void launch_softmax_rows(float* x, int rows, int width, cudaStream_t st) {
+    if (width <= 256) softmax_rows_kernel<1><<<rows, 256, 0, st>>>(x, width);
+    else if (width <= 1024) softmax_rows_kernel<4><<<rows, 256, 0, st>>>(x, width);
+    else if (width <= 4096) softmax_rows_kernel<16><<<rows, 256, 0, st>>>(x, width);
+    else if (width <= 8192) softmax_rows_kernel<32><<<rows, 256, 0, st>>>(x, width);
+    else softmax_rows_wide_kernel<<<rows, 256, 0, st>>>(x, width);
+}
+
+// ---------------------------------------------- attention scores / values --
+
+// Thread per position: sequential dot product in the reference order, then
+// the scale (Attention.java:33-41).  Bit-identical to the Java loop.
+__global__ void attn_scores_kernel(const float* __restrict__ q, const float* __restrict__ keys,
+                                   float* __restrict__ scores, int seq_len, int head_dim, float scale) {
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < seq_len; t += gridDim.x * blockDim.x) {
+        const float* k = keys + (size_t)t * head_dim;
+        float sum = 0.0f;
+        for (int i = 0; i < head_dim; ++i) sum = __fadd_rn(sum, __fmul_rn(q[i], k[i]));
+        scores[t] = __fmul_rn(sum, scale);
+    }
+}
+
+// Thread per output dimension: sequential sum over positions in the reference
+// order (Attention.java:54-60).  Bit-identical to the Java loop.
+__global__ void attn_values_kernel(const float* __restrict__ p, const float* __restrict__ values,
+                                   float* __restrict__ out, int seq_len, int head_dim) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < head_dim; i += gridDim.x * blockDim.x) {
+        float sum = 0.0f;
+        for (int t = 0; t < seq_len; ++t) sum = __fadd_rn(sum, __fmul_rn(p[t], values[(size_t)t * head_dim + i]));
+        out[i] = sum;
+    }
+}
+
+void launch_attn_scores(const float* q, const float* keys, float* scores, int seq_len, int head_dim, float scale,
+                        cudaStream_t st) {
+    int blocks = (seq_len + 255) / 256;
+    if (blocks < 1) blocks = 1;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    attn_scores_kernel<<<blocks, 256, 0, st>>>(q, keys, scores, seq_len, head_dim, scale);
+}
+
+void launch_attn_values(const float* p, const float* values, float* out, int seq_len, int head_dim,
+                        cudaStream_t st) {
+    int blocks = (head_dim + 63) / 64;
+    attn_values_kernel<<<blocks, 64, 0, st>>>(p, values, out, seq_len, head_dim);
+}
+
+// ---------------------------------------------------------------- argmax --
+
+// Single CTA: each thread scans its strided indices in increasing order with
+// strict '>' (first occurrence), then candidates merge by (value desc, index
+// asc).  NaNs never win; values[0] == NaN yields 0 as in the Java loop.
+__global__ void argmax_kernel(const float* __restrict__ v, int n, int32_t* __restrict__ out) {
+    __shared__ float bv_s[32];
+    __shared__ int bi_s[32];
+    float bv = -INFINITY;
+    int bi = -1;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float x = v[i];
+        if (x == x && (bi < 0 || x > bv)) {
+            bv = x;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+        int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        argmax_merge(bv, bi, v2, i2);
+    }
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        bv_s[w] = bv;
+        bi_s[w] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float B = bv_s[0];
+        int I = bi_s[0];
+        for (int k = 1; k < (int)(blockDim.x >> 5); ++k) argmax_merge(B, I, bv_s[k], bi_s[k]);
+        const float v0 = v[0];
+        *out = (v0 != v0 || I < 0) ? 0 : I;
+    }
+}
+
+void launch_argmax(const float* v, int n, int32_t* out, cudaStream_t st) { argmax_kernel<<<1, 1024, 0, st>>>(v, n, out); }
+
+}  // namespace lc

@@ -1,0 +1,20 @@
+"""llamahat -- B200 (sm_100a) CUDA implementation of the llama3-java-hat decode path.
+
+Python host mirror of the reference's kernel strategy API (`CudaKernelFactory`)
+and inference driver (`LlamaInference`) over the C ABI of libllamacuda.so.
+"""
+from ._lib import (DeviceTimeoutError, IllegalArgumentError, IllegalStateError, LlamaCudaError, ModelIOError,
+                   load as load_library)
+from .config import LLAMA_3_2_1B, TINY, LlamaConfig
+from .kernels import (Accelerator, CudaAttention, CudaGEMV, CudaKernelFactory, CudaRMSNorm, CudaRoPE, CudaSiLU,
+                      CudaSoftmax, IAttention, IGEMV, IKernelFactory, IRMSNorm, IRoPE, ISiLU, ISoftmax,
+                      default_accelerator)
+from .inference import EOS_TOKEN, CudaModel, LlamaInference, Session
+
+__all__ = [
+    "Accelerator", "CudaAttention", "CudaGEMV", "CudaKernelFactory", "CudaModel", "CudaRMSNorm", "CudaRoPE",
+    "CudaSiLU", "CudaSoftmax", "DeviceTimeoutError", "EOS_TOKEN", "IAttention", "IGEMV", "IKernelFactory",
+    "IRMSNorm", "IRoPE", "ISiLU", "ISoftmax", "IllegalArgumentError", "IllegalStateError", "LLAMA_3_2_1B",
+    "LlamaConfig", "LlamaCudaError", "LlamaInference", "ModelIOError", "Session", "TINY", "default_accelerator",
+    "load_library",
+]

@@ -1,0 +1,131 @@
+"""Device-resident model and the LlamaInference mirror.
+
+Reference: src/main/java/com/arturskowronski/llama3babylon/hat/LlamaInference.java
+  ctor :58-100, forward(token, pos) :117-164, generate(prompt, maxNew[, stop]) :173-217,
+  argmax :252-262.
+
+`LlamaInference` keeps the reference's call surface.  Weights are uploaded
+to the GPU once (`CudaModel`); each `forward` is one launch of the fused decode
+kernel; `generate` runs the whole prefill + greedy loop in one launch and
+copies back only the generated token ids.
+"""
+from __future__ import annotations
+
+import ctypes
+import weakref
+
+import numpy as np
+
+from . import _lib
+from .config import LlamaConfig
+from .kernels import Accelerator, _addr, default_accelerator
+
+EOS_TOKEN = 128001  # LlamaInference.java:174
+
+
+class CudaModel:
+    """Weights in HBM (one arena) plus the prepared decode kernel."""
+
+    def __init__(self, cfg: LlamaConfig | None = None, weights: dict | None = None, gguf_path: str | None = None,
+                 acc: Accelerator | None = None, max_seq: int = 0):
+        self.acc = acc or default_accelerator()
+        lib = _lib.load()
+        h = ctypes.c_void_p()
+        if gguf_path is not None:
+            _lib.check(lib.lc_model_load_gguf(self.acc.handle, gguf_path.encode(), max_seq, ctypes.byref(h)))
+            c = _lib.LcConfig()
+            _lib.check(lib.lc_model_get_config(h, ctypes.byref(c)))
+            self.cfg = LlamaConfig.from_lc(c)
+        else:
+            if cfg is None or weights is None:
+                raise ValueError("need cfg and weights, or gguf_path")
+            self.cfg = cfg
+            lc = cfg.to_lc()
+            _lib.check(lib.lc_model_create(self.acc.handle, ctypes.byref(lc), ctypes.byref(h)))
+        self.handle = h
+        self._fin = weakref.finalize(self, lib.lc_model_destroy, h)
+        if gguf_path is None:
+            for name, a in weights.items():
+                self.upload(name, a)
+            _lib.check(lib.lc_model_finalize(h))
+
+    def upload(self, name: str, a) -> None:
+        lib = _lib.load()
+        if isinstance(a, np.ndarray):
+            dtype = 1 if a.dtype in (np.float16, np.uint16) else 0
+            a = np.ascontiguousarray(a)
+            _lib.check(lib.lc_model_upload_tensor(self.handle, name.encode(), a.ctypes.data, a.size, dtype))
+        else:  # torch tensor (host or device)
+            dtype = 1 if str(a.dtype) in ("torch.float16", "torch.int16") else 0
+            _lib.check(lib.lc_model_upload_tensor(self.handle, name.encode(), a.contiguous().data_ptr(), a.numel(), dtype))
+
+    def close(self) -> None:
+        self._fin()
+
+
+class Session:
+    """One decoding sequence: device KV cache + activations."""
+
+    def __init__(self, model: CudaModel):
+        self.model = model
+        lib = _lib.load()
+        h = ctypes.c_void_p()
+        _lib.check(lib.lc_session_create(model.handle, ctypes.byref(h)))
+        self.handle = h
+        self._fin = weakref.finalize(self, lib.lc_session_destroy, h)
+
+    def forward(self, token: int, pos: int, logits=None) -> tuple[np.ndarray | None, int]:
+        lib = _lib.load()
+        am = np.zeros(1, np.int32)
+        lp = None if logits is None else _addr(logits, "f32", self.model.cfg.vocab, True)
+        _lib.check(lib.lc_forward(self.handle, int(token), int(pos), lp, am.ctypes.data))
+        return logits, int(am[0])
+
+    def generate(self, prompt, max_new: int, stop=(EOS_TOKEN,)) -> np.ndarray:
+        lib = _lib.load()
+        p = np.ascontiguousarray(np.asarray(prompt, dtype=np.int32))
+        st = np.ascontiguousarray(np.asarray(sorted(stop) if stop else [], dtype=np.int32))
+        out = np.zeros(max(max_new, 1), np.int32)
+        n = np.zeros(1, np.int32)
+        _lib.check(lib.lc_generate(self.handle, p.ctypes.data, p.size, int(max_new),
+                                   st.ctypes.data if st.size else None, st.size, out.ctypes.data, n.ctypes.data))
+        return out[: int(n[0])].copy()
+
+    def decode(self, token: int, start_pos: int, n_steps: int, out=None) -> np.ndarray:
+        lib = _lib.load()
+        o = out if out is not None else np.zeros(n_steps, np.int32)
+        _lib.check(lib.lc_decode(self.handle, int(token), int(start_pos), int(n_steps), _addr(o, "i32", n_steps, True)))
+        return o
+
+    def last_ms(self) -> float:
+        v = ctypes.c_float()
+        _lib.check(_lib.load().lc_session_last_ms(self.handle, ctypes.byref(v)))
+        return float(v.value)
+
+    def close(self) -> None:
+        self._fin()
+
+
+class LlamaInference:
+    """Mirror of LlamaInference (LlamaInference.java): forward / generate / argmax."""
+
+    def __init__(self, model: CudaModel | str, acc: Accelerator | None = None, max_seq: int = 0):
+        self.model = model if isinstance(model, CudaModel) else CudaModel(gguf_path=model, acc=acc, max_seq=max_seq)
+        self.session = Session(self.model)
+        self.cfg = self.model.cfg
+
+    def forward(self, token: int, pos: int) -> np.ndarray:
+        """Logits [vocab] for `token` at `pos` (LlamaInference.java:117-164)."""
+        logits = np.empty(self.cfg.vocab, np.float32)
+        self.session.forward(token, pos, logits)
+        return logits
+
+    def generate(self, promptTokens, maxNewTokens: int, stopTokens=frozenset({EOS_TOKEN})) -> np.ndarray:
+        """Greedy generation (LlamaInference.java:173-217)."""
+        return self.session.generate(promptTokens, maxNewTokens, tuple(stopTokens))
+
+    @staticmethod
+    def argmax(values) -> int:
+        """First index of the maximum (LlamaInference.java:252-262), computed on the GPU."""
+        from .kernels import argmax as _am
+        return _am(np.ascontiguousarray(np.asarray(values, dtype=np.float32)))

@@ -1,0 +1,212 @@
+"""End-to-end parity of the fused decode path (one launch per forward /
+generate) against the oracle, error behaviour of the model API, the GGUF
+loader, and the per-kernel factory path (the reference's own orchestration
+driving CudaKernelFactory).  All calls go through the C ABI."""
+import os
+
+import numpy as np
+import pytest
+
+from parity import LOGITS_ABS_TOL, MARGIN, assert_kernel_close, max_rel_err, top2_margin
+
+pytestmark = pytest.mark.gpu
+f32 = np.float32
+
+
+@pytest.fixture(scope="module")
+def tiny(acc, tiny_weights):
+    from llamahat import CudaModel
+    cfg, w = tiny_weights
+    return cfg, w, CudaModel(cfg, w, acc=acc)
+
+
+def test_tiny_forward_matches_oracle(tiny, oracle):
+    from llamahat import LlamaInference
+    cfg, w, model = tiny
+    inf = LlamaInference(model)
+    om = oracle.OracleModel(cfg, w)
+    toks = [3, 17, 999, 0, 512, 5, 5, 700, 1, 2, 3, 4]
+    for pos, t in enumerate(toks):
+        g, r = inf.forward(t, pos), om.forward(t, pos)
+        assert np.abs(g - r).max() <= LOGITS_ABS_TOL
+        assert_kernel_close(g, r)
+        if top2_margin(r) > MARGIN:
+            assert int(np.argmax(g)) == oracle.argmax(r)
+
+
+def test_tiny_generate_matches_oracle(tiny, oracle):
+    from llamahat import LlamaInference
+    cfg, w, model = tiny
+    prompt = [11, 22, 33, 44, 55, 66, 77, 88]
+    gen = LlamaInference(model).generate(prompt, 20, stopTokens=())
+    ref = oracle.OracleModel(cfg, w).generate(prompt, 20, stop=())
+    assert list(gen) == list(ref)
+
+
+def test_tiny_generate_stop_token(tiny, oracle):
+    from llamahat import LlamaInference
+    cfg, w, model = tiny
+    prompt = [101, 202, 303]
+    free = oracle.OracleModel(cfg, w).generate(prompt, 10, stop=())
+    stop = int(free[2])
+    gen = LlamaInference(model).generate(prompt, 10, stopTokens={stop})
+    first = list(free).index(stop)
+    assert list(gen) == list(free[:first + 1])
+
+
+def test_tiny_decode_continues_generate(tiny):
+    from llamahat import Session
+    cfg, w, model = tiny
+    prompt = [9, 8, 7, 6]
+    s1 = Session(model)
+    full = s1.generate(prompt, 12, stop=())
+    s2 = Session(model)
+    head = s2.generate(prompt, 4, stop=())
+    tail = s2.decode(int(head[-1]), len(prompt) + 3, 8)
+    assert list(head) + list(tail) == list(full)
+
+
+def test_forward_sessions_are_independent(tiny):
+    from llamahat import LlamaInference
+    cfg, w, model = tiny
+    a, b = LlamaInference(model), LlamaInference(model)
+    la = a.forward(5, 0)
+    b.forward(6, 0)
+    b.forward(7, 1)
+    assert np.array_equal(a.forward(5, 0), la)
+
+
+def test_gguf_roundtrip_load(tiny, tmp_path, acc):
+    from llamahat import CudaModel, LlamaInference
+    from llamahat.gguf import read_gguf, write_gguf
+    cfg, w, model = tiny
+    path = str(tmp_path / "tiny.gguf")
+    write_gguf(path, cfg, w)
+    meta, tensors = read_gguf(path)
+    assert meta["general.architecture"] == "llama"
+    assert np.array_equal(tensors["blk.1.ffn_down.weight"], w["blk.1.ffn_down.weight"])
+    loaded = CudaModel(gguf_path=path, acc=acc, max_seq=cfg.max_seq)
+    assert loaded.cfg.dim == cfg.dim and loaded.cfg.vocab == cfg.vocab and loaded.cfg.n_layers == cfg.n_layers
+    g1 = LlamaInference(loaded).forward(42, 0)
+    g2 = LlamaInference(model).forward(42, 0)
+    assert np.array_equal(g1, g2)
+
+
+def test_model_errors(tiny, acc, tmp_path):
+    from llamahat import CudaModel, IllegalArgumentError, LlamaInference, ModelIOError
+    cfg, w, model = tiny
+    inf = LlamaInference(model)
+    with pytest.raises(IllegalArgumentError):
+        inf.forward(cfg.vocab, 0)            # token outside the vocabulary
+    with pytest.raises(IllegalArgumentError):
+        inf.forward(1, cfg.max_seq)          # position past the KV cache
+    with pytest.raises(IllegalArgumentError):
+        inf.generate([], 4)                  # empty prompt
+    with pytest.raises(IllegalArgumentError):
+        inf.generate([1], 0)
+    with pytest.raises(IllegalArgumentError):
+        inf.generate([1] * 10, cfg.max_seq)  # past max_seq
+    # The context stays usable after rejected calls.
+    assert np.isfinite(inf.forward(1, 0)).all()
+    part = {k: v for k, v in w.items() if k != "blk.1.ffn_up.weight"}
+    with pytest.raises(ModelIOError, match="blk.1.ffn_up.weight"):
+        CudaModel(cfg, part, acc=acc)        # missing tensor at finalize
+    bad = dict(w)
+    bad["blk.0.attn_q.weight"] = w["blk.0.attn_q.weight"][:-1]
+    with pytest.raises(ModelIOError, match="Shape mismatch"):
+        CudaModel(cfg, bad, acc=acc)
+    bad = dict(w)
+    bad["blk.0.attn_k.weight"] = w["blk.0.attn_k.weight"].astype(f32)
+    with pytest.raises(IllegalArgumentError, match="Expected F16"):
+        CudaModel(cfg, bad, acc=acc)
+    p = tmp_path / "notgguf.bin"
+    p.write_bytes(b"\0" * 64)
+    with pytest.raises(ModelIOError):
+        CudaModel(gguf_path=str(p), acc=acc)
+
+
+def test_factory_path_matches_oracle(tiny, oracle, acc):
+    """The reference's TransformerBlock/LlamaInference orchestration, with
+    every kernel call served by CudaKernelFactory, against the oracle."""
+    from llamahat import CudaKernelFactory
+    from llamahat.factory_path import FactoryLlamaInference
+    cfg, w, model = tiny
+    fi = FactoryLlamaInference(cfg, w, CudaKernelFactory(), acc)
+    om = oracle.OracleModel(cfg, w)
+    for pos, t in enumerate([4, 400, 40, 4]):
+        g, r = fi.forward(t, pos), om.forward(t, pos)
+        assert np.abs(g - r).max() <= LOGITS_ABS_TOL
+        assert_kernel_close(g, r)
+
+
+def test_transformer_block_fixture_random42(oracle, acc):
+    """TransformerBlockTest.testForwardPassWithGQA (TransformerBlockTest.java:72-147):
+    the same java.util.Random(42) weights and input, one Llama-3.2-1B block at
+    position 0 through CudaKernelFactory; the reference asserts a finite,
+    non-zero output -- here it must also match the oracle."""
+    from java_random import JavaRandom, random_array
+    from llamahat import CudaKernelFactory, LLAMA_3_2_1B
+    from llamahat.factory_path import FactoryTransformerBlock
+    cfg = LLAMA_3_2_1B.with_(n_layers=1, vocab=2, max_seq=16)
+    H, I, KV = cfg.dim, cfg.hidden, cfg.kv_dim
+    rng = JavaRandom(42)
+    spec = [("attn_norm", H, 0.1, f32), ("attn_q", H * H, 0.01, np.float16), ("attn_k", H * KV, 0.01, np.float16),
+            ("attn_v", H * KV, 0.01, np.float16), ("attn_output", H * H, 0.01, np.float16), ("ffn_norm", H, 0.1, f32),
+            ("ffn_gate", I * H, 0.01, np.float16), ("ffn_down", H * I, 0.01, np.float16), ("ffn_up", I * H, 0.01, np.float16)]
+    shapes = {"attn_q": (H, H), "attn_k": (KV, H), "attn_v": (KV, H), "attn_output": (H, H),
+              "ffn_gate": (I, H), "ffn_down": (H, I), "ffn_up": (I, H)}
+    w = {}
+    for name, n, scale, dt in spec:
+        a = random_array(rng, n, scale).astype(dt)
+        w[f"blk.0.{name}.weight"] = a.reshape(shapes[name]) if name in shapes else a
+    x = rng.next_floats(H) * np.float32(0.1)
+    w["token_embd.weight"] = np.zeros((2, H), np.float16)
+    w["output_norm.weight"] = np.ones(H, f32)
+    blk = FactoryTransformerBlock(cfg, w, 0, CudaKernelFactory(), acc)
+    xg = x.copy()
+    blk.forward(xg, 0, np.zeros(cfg.max_seq * KV, f32), np.zeros(cfg.max_seq * KV, f32))
+    assert np.all(np.isfinite(xg)) and np.any(xg != 0)
+    xr = oracle.OracleModel(cfg, w).block_forward(0, x, 0)
+    assert_kernel_close(xg, xr)
+
+
+@pytest.fixture(scope="module")
+def full_model(acc):
+    from llamahat import LLAMA_3_2_1B, CudaModel
+    from llamahat.synth import synth_weights
+    w = synth_weights(LLAMA_3_2_1B, seed=1234)
+    return LLAMA_3_2_1B, w, CudaModel(LLAMA_3_2_1B, w, acc=acc)
+
+
+def test_llama_1b_generate_matches_oracle(full_model, oracle):
+    """The headline workload: 16-token prompt, 32-token greedy decode."""
+    from llamahat import LlamaInference
+    from llamahat.synth import synth_prompt
+    cfg, w, model = full_model
+    prompt = synth_prompt(16, seed=1234)
+    om = oracle.OracleModel(cfg, w)
+    ref_logits = []
+    for i, t in enumerate(prompt):
+        lg = om.forward(int(t), i)
+    toks = [oracle.argmax(lg)]
+    ref_logits.append(lg)
+    while len(toks) < 32:
+        lg = om.forward(toks[-1], len(prompt) + len(toks) - 1)
+        ref_logits.append(lg)
+        toks.append(oracle.argmax(lg))
+    gen = LlamaInference(model).generate(prompt, 32, stopTokens=())
+    assert len(gen) == 32
+    # Tokens must agree wherever the oracle's top-2 margin exceeds 1e-2; the
+    # first disagreement may only come at a near-tie, after which sequences
+    # legitimately diverge.
+    for i, (g, r) in enumerate(zip(gen, toks)):
+        if g != r:
+            assert top2_margin(ref_logits[i]) <= MARGIN, f"token {i}: {g} vs {r}"
+            break
+    # Logits of the forward path at the final position.
+    inf = LlamaInference(model)
+    seq = list(prompt) + toks[:-1]
+    for pos, t in enumerate(seq):
+        lg_gpu = inf.forward(int(t), pos)
+    assert np.abs(lg_gpu - ref_logits[-1]).max() <= LOGITS_ABS_TOL
+    assert_kernel_close(lg_gpu, ref_logits[-1])

@@ -136,6 +136,21 @@ int lc_attention_decode(lc_context* ctx, const float* q, const float* k, const f
                         const int32_t* seq_len, int batch, int n_heads, int n_kv_heads, int head_dim,
                         int64_t seq_stride, int64_t head_stride, int64_t pos_stride);
 
+/* lc_attention_decode without any device allocation.  No counterpart in the
+ * reference.  For hosts that cannot call cudaMalloc at this point (device
+ * memory owned by the host's own pool allocator, latency-critical loops that
+ * cannot afford cudaFree's device-wide synchronisation, fixed device
+ * footprint after load).  Same arguments and results as lc_attention_decode;
+ * q, k, v and out must be device memory of the context's device; seq_len may
+ * be host or device.  Scratch is a static 8 MiB device array per GPU (held
+ * until exit); plans needing more, or batch > 1024, return LC_ERR_INVALID_ARG.
+ * The first call on a device resolves the array's address (make it before
+ * any stream capture).  All calls on a device share the array: calls that
+ * overlap on the GPU race.  Enqueues on the context stream and returns. */
+int lc_attention_decode_static(lc_context* ctx, const float* q, const float* k, const float* v, float* out,
+                               const int32_t* seq_len, int batch, int n_heads, int n_kv_heads, int head_dim,
+                               int64_t seq_stride, int64_t head_stride, int64_t pos_stride);
+
 /* LlamaInference.argmax(values) H/LlamaInference.java:252-262: first index of
  * the maximum (ties -> lowest index; 0 when values[0] is NaN). */
 int lc_argmax(lc_context* ctx, const float* values, int n, int32_t* out_index);

@@ -949,3 +949,12 @@ extern "C" int lc_session_last_ms(lc_session* s, float* ms) {
 extern "C" __attribute__((visibility("hidden"))) int lc_gguf_set_error(int code, const char* msg) {
     return fail(code, "%s", msg);
 }
+
+// Accessors for lc_attention_static.cu (not part of the public ABI).
+extern "C" __attribute__((visibility("hidden"))) int lc_internal_set_error(int code, const char* msg) {
+    return fail(code, "%s", msg);
+}
+
+extern "C" __attribute__((visibility("hidden"))) int lc_internal_context_device(const lc_context* c) {
+    return c ? c->device : -1;
+}

@@ -92,6 +92,8 @@ SIGNATURES = {
     "lc_attn_values": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]),
     "lc_attention_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                     c_int, c_int, c_int64, c_int64, c_int64]),
+    "lc_attention_decode_static": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                           c_int, c_int, c_int, c_int64, c_int64, c_int64]),
     "lc_argmax": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
     "lc_config_llama32_1b": (None, [POINTER(LcConfig)]),
     "lc_model_create": (c_int, [c_void_p, POINTER(LcConfig), POINTER(c_void_p)]),

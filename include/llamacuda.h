@@ -225,6 +225,17 @@ int lc_generate(lc_session* s, const int32_t* prompt, int32_t n_prompt, int32_t 
  * lc_generate runs after the prompt. */
 int lc_decode(lc_session* s, int32_t token, int32_t start_pos, int32_t n_steps, int32_t* out_tokens);
 
+/* Phase trace of the fused decode kernel (diagnostics).  words_per_cta > 0
+ * allocates a [grid][words_per_cta] uint64 buffer (0 frees it); while set,
+ * every launch records %globaltimer stamps: per CTA, the first half holds
+ * consumer marks (per layer: QKV start / consumed / barrier, attention done /
+ * barrier, then start / consumed / barrier for O, gate-up and down; per
+ * lm_head step: start / consumed / barrier / argmax), the second half one
+ * producer mark per weight job (last stage issued).  Read with
+ * lc_session_read_trace (grid and words_per_cta may be NULL). */
+int lc_session_enable_trace(lc_session* s, int32_t words_per_cta);
+int lc_session_read_trace(lc_session* s, uint64_t* out, int64_t n_words, int32_t* grid, int32_t* words_per_cta);
+
 /* Device time of the last lc_generate / lc_decode / lc_forward launch in ms
  * (CUDA events on the session stream). */
 int lc_session_last_ms(lc_session* s, float* ms);

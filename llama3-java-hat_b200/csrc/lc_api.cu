@@ -8,6 +8,7 @@
 #include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <string>
@@ -495,9 +496,11 @@ struct lc_model {
     lc_config cfg;
     void* arena = nullptr;  // all weights, one allocation
     size_t arena_bytes = 0;
-    __half* tok_emb = nullptr;
-    __half* out_w = nullptr;  // only if "output.weight" is uploaded
+    __half* tok_emb = nullptr;   // row-major (embedding lookup)
+    __half* lm_tiled = nullptr;  // tiled lm_head: output.weight, or tok_emb when tied
     float* out_norm = nullptr;
+    void* staging = nullptr;     // device copy of a host matrix before tiling
+    size_t staging_bytes = 0;
     std::vector<LayerStore> layers;
     LayerW* d_layers = nullptr;
     std::vector<uint8_t> have;  // received flags
@@ -505,6 +508,7 @@ struct lc_model {
     bool finalized = false;
     RopeFreq rope;
     DecodeLaunch launch;
+    int l2_prefetch_stages = 0;  // producer L2 prefetch distance (tiles)
 };
 
 static int validate_config(const lc_config* c) {
@@ -533,7 +537,9 @@ extern "C" int lc_model_create(lc_context* ctx, const lc_config* cfg, lc_model**
     auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
     size_t per_layer = al((qdim + 2 * kvd) * c.dim * 2) + al((size_t)c.dim * qdim * 2) +
                        al((size_t)2 * c.hidden * c.dim * 2) + al((size_t)c.dim * c.hidden * 2) + 2 * al((size_t)c.dim * 4);
-    size_t total = al((size_t)c.vocab * c.dim * 2) + al((size_t)c.dim * 4) + per_layer * c.n_layers;
+    const size_t vocab8 = ((size_t)c.vocab + 7) / 8 * 8;
+    size_t total = al((size_t)c.vocab * c.dim * 2) + al(vocab8 * c.dim * 2) + al((size_t)c.dim * 4) +
+                   per_layer * c.n_layers;
     cudaError_t e = cudaMalloc(&m->arena, total);
     if (e != cudaSuccess) {
         delete m;
@@ -547,6 +553,7 @@ extern "C" int lc_model_create(lc_context* ctx, const lc_config* cfg, lc_model**
         return r;
     };
     m->tok_emb = (__half*)take((size_t)c.vocab * c.dim * 2);
+    m->lm_tiled = (__half*)take(vocab8 * c.dim * 2);
     m->out_norm = (float*)take((size_t)c.dim * 4);
     m->layers.resize(c.n_layers);
     for (int l = 0; l < c.n_layers; ++l) {
@@ -559,6 +566,12 @@ extern "C" int lc_model_create(lc_context* ctx, const lc_config* cfg, lc_model**
         L.ffn_norm = (float*)take((size_t)c.dim * 4);
     }
     m->have.assign(kLayerBase + kPerLayer * c.n_layers, 0);
+    // Padding rows of the tiled lm_head must read as zeros.
+    e = cudaMemset(m->lm_tiled, 0, vocab8 * c.dim * 2);
+    if (e != cudaSuccess) {
+        lc_model_destroy(m);
+        return cuda_fail(e, "weight arena");
+    }
     *out = m;
     return LC_OK;
 }
@@ -573,7 +586,7 @@ extern "C" int lc_model_destroy(lc_model* m) {
     if (!m) return LC_OK;
     cudaSetDevice(m->ctx->device);
     if (m->arena) cudaFree(m->arena);
-    if (m->out_w) cudaFree(m->out_w);
+    if (m->staging) cudaFree(m->staging);
     if (m->d_layers) cudaFree(m->d_layers);
     delete m;
     return LC_OK;
@@ -594,6 +607,32 @@ static float f16_bits_to_float(uint16_t h) {
 // Copies `bytes` from a host or device source into device memory.
 static int put(void* dst, const void* src, size_t bytes, cudaStream_t st) {
     CK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, st), "tensor upload");
+    return LC_OK;
+}
+
+// Row-major F16 matrix [rows][cols] from a host or device source into the
+// tiled layout of a destination matrix with `cols` columns (lc_internal.h):
+// source row r becomes destination row row0 + r * row_step.
+static int put_tiled(lc_model* m, __half* dst, const void* data, int rows, int cols, int row0, int row_step) {
+    cudaStream_t st = m->ctx->stream;
+    const size_t bytes = (size_t)rows * cols * 2;
+    cudaPointerAttributes a;
+    const __half* src = (const __half*)data;
+    const bool on_device = cudaPointerGetAttributes(&a, data) == cudaSuccess && a.type == cudaMemoryTypeDevice &&
+                           a.device == m->ctx->device && ((uintptr_t)data & 15) == 0;
+    cudaGetLastError();
+    if (!on_device) {
+        if (m->staging_bytes < bytes) {
+            if (m->staging) cudaFree(m->staging);
+            m->staging = nullptr;
+            m->staging_bytes = 0;
+            CK(cudaMalloc(&m->staging, bytes), "weight staging buffer");
+            m->staging_bytes = bytes;
+        }
+        CK(cudaMemcpyAsync(m->staging, data, bytes, cudaMemcpyDefault, st), "tensor upload");
+        src = (const __half*)m->staging;
+    }
+    CK(launch_tile_rows(src, dst, rows, cols, m->cfg.dim, row0, row_step, st), "weight tiling");
     return LC_OK;
 }
 
@@ -630,12 +669,11 @@ extern "C" int lc_model_upload_tensor(lc_model* m, const char* name, const void*
     if (!strcmp(name, "token_embd.weight") || !strcmp(name, "output.weight")) {
         if ((rc = need_f16()) || (rc = expect((int64_t)c.vocab * c.dim))) return rc;
         const bool out_w = name[0] == 'o';
-        __half* dst = m->tok_emb;
         if (out_w) {
-            if (!m->out_w) CK(cudaMalloc(&m->out_w, (size_t)c.vocab * c.dim * 2), "output.weight");
-            dst = m->out_w;
+            if ((rc = put_tiled(m, m->lm_tiled, data, c.vocab, c.dim, 0, 1))) return rc;
+        } else if ((rc = put(m->tok_emb, data, (size_t)n * 2, st))) {
+            return rc;
         }
-        if ((rc = put(dst, data, (size_t)n * 2, st))) return rc;
         m->have[out_w ? kOutput : kTokEmb] = 1;
         m->has_output |= out_w;
     } else if (!strcmp(name, "output_norm.weight")) {
@@ -659,24 +697,21 @@ extern "C" int lc_model_upload_tensor(lc_model* m, const char* name, const void*
             const int64_t rows = (t[5] == 'q') ? qdim : kvd;
             if ((rc = need_f16()) || (rc = expect(rows * c.dim))) return rc;
             const int64_t row0 = (t[5] == 'q') ? 0 : (t[5] == 'k') ? qdim : qdim + kvd;
-            if ((rc = put(L.wqkv + row0 * c.dim, data, (size_t)n * 2, st))) return rc;
+            if ((rc = put_tiled(m, L.wqkv, data, (int)rows, c.dim, (int)row0, 1))) return rc;
             slot = (t[5] == 'q') ? kQ : (t[5] == 'k') ? kK : kV;
         } else if (!strcmp(t, "attn_output.weight")) {
             if ((rc = need_f16()) || (rc = expect((int64_t)c.dim * qdim))) return rc;
-            if ((rc = put(L.wo, data, (size_t)n * 2, st))) return rc;
+            if ((rc = put_tiled(m, L.wo, data, c.dim, (int)qdim, 0, 1))) return rc;
             slot = kO;
         } else if (!strcmp(t, "ffn_gate.weight") || !strcmp(t, "ffn_up.weight")) {
             if ((rc = need_f16()) || (rc = expect((int64_t)c.hidden * c.dim))) return rc;
             // Row r of gate -> row 2r of the packed matrix, row r of up -> 2r+1.
             const bool up = t[4] == 'u';
-            const size_t rowb = (size_t)c.dim * 2;
-            CK(cudaMemcpy2DAsync((uint8_t*)L.wgu + (up ? rowb : 0), 2 * rowb, data, rowb, rowb, (size_t)c.hidden,
-                                 cudaMemcpyDefault, st),
-               "gate/up upload");
+            if ((rc = put_tiled(m, L.wgu, data, c.hidden, c.dim, up ? 1 : 0, 2))) return rc;
             slot = up ? kUp : kGate;
         } else if (!strcmp(t, "ffn_down.weight")) {
             if ((rc = need_f16()) || (rc = expect((int64_t)c.dim * c.hidden))) return rc;
-            if ((rc = put(L.wdown, data, (size_t)n * 2, st))) return rc;
+            if ((rc = put_tiled(m, L.wdown, data, c.dim, c.hidden, 0, 1))) return rc;
             slot = kDown;
         } else {
             return fail(LC_ERR_NOT_FOUND, "Tensor not found: %s", name);
@@ -714,11 +749,12 @@ static void fill_model_params(const lc_model* m, DecodeParams* p) {
     p->eps = c.rms_eps;
     p->attn_scale = 1.0f / (float)sqrt((double)c.head_dim);  // Attention.java:33
     p->tok_emb = m->tok_emb;
-    p->lm_head = m->has_output ? m->out_w : m->tok_emb;      // tied, LlamaInference.java:69-72
+    p->lm_head = m->lm_tiled;  // output.weight, or the tied embedding (LlamaInference.java:69-72)
     p->out_norm = m->out_norm;
     p->layers = m->d_layers;
     p->rope = m->rope;
     p->timeout_ns = 2000000000ull;
+    p->l2_prefetch_stages = m->l2_prefetch_stages;
 }
 
 extern "C" int lc_model_finalize(lc_model* m) {
@@ -730,7 +766,17 @@ extern "C" int lc_model_finalize(lc_model* m) {
         if (s == kOutput) continue;  // optional: tied embeddings
         if (!m->have[s]) return fail(LC_ERR_NOT_FOUND, "Tensor not found: %s", slot_name((int)s, buf));
     }
+    // Tied embeddings: the lm_head is the token embedding (LlamaInference.java:69-72).
+    if (!m->has_output) {
+        int rc = put_tiled(m, m->lm_tiled, m->tok_emb, m->cfg.vocab, m->cfg.dim, 0, 1);
+        if (rc) return rc;
+    }
+    CK(cudaStreamSynchronize(m->ctx->stream), "weight tiling");
+    if (m->staging) cudaFree(m->staging);
+    m->staging = nullptr;
+    m->staging_bytes = 0;
     make_rope_freq(&m->rope, m->cfg.rope_theta, m->cfg.head_dim);
+    if (const char* e = getenv("LLAMACUDA_L2_PREFETCH_STAGES")) m->l2_prefetch_stages = atoi(e);
     std::vector<LayerW> lw(m->cfg.n_layers);
     for (int l = 0; l < m->cfg.n_layers; ++l) {
         const LayerStore& L = m->layers[l];
@@ -752,14 +798,17 @@ extern "C" int lc_model_finalize(lc_model* m) {
 struct lc_session {
     lc_model* m = nullptr;
     void* mem = nullptr;
-    float *kcache, *vcache, *x, *qbuf, *att, *hbuf, *logits, *attn_part, *amax_val;
-    uint32_t *attn_cnt, *bar;
-    int *amax_idx, *err, *n_done;
+    float *xa, *xb, *q, *att, *part, *h, *amax;
+    uint32_t* flags;
+    float *kcache, *vcache, *logits;
+    int *err, *n_done;
     int32_t* tokens;
     int attn_max_splits = 0;
     int32_t* pinned = nullptr;  // host staging for small transfers
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.0f;
+    unsigned long long* trace = nullptr;  // phase trace buffer (debug), grid x trace_words
+    int trace_words = 0;
 };
 
 extern "C" int lc_session_create(lc_model* m, lc_session** out) {
@@ -770,14 +819,26 @@ extern "C" int lc_session_create(lc_model* m, lc_session** out) {
     lc_session* s = new lc_session();
     s->m = m;
     const int kv_mul = c.n_heads / c.n_kv_heads;
-    s->attn_max_splits = (c.max_seq + 63) / 64;
+    s->attn_max_splits = decode_attn_max_splits(c.max_seq, m->launch.grid, c.n_kv_heads);
     const size_t G = (size_t)m->launch.grid;
     auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
+    const size_t qd = (size_t)c.n_heads * c.head_dim;
     const size_t kv = (size_t)c.n_layers * c.n_kv_heads * c.max_seq * c.head_dim * 4;
-    const size_t qd = (size_t)c.n_heads * c.head_dim * 4;
-    size_t sizes[] = {kv, kv, (size_t)c.dim * 4, qd, qd, (size_t)c.hidden * 4, (size_t)c.vocab * 4,
-                      (size_t)c.n_kv_heads * s->attn_max_splits * kv_mul * kAttnPartStride * 4, G * 4,
-                      (size_t)c.n_kv_heads * 4, 4, G * 4, 4, 4, (size_t)(c.max_seq + 1) * 4};
+    const size_t sizes[] = {(size_t)c.dim * 4,
+                            (size_t)c.dim * 4,
+                            qd * 4,
+                            qd * 4,
+                            (size_t)c.n_kv_heads * s->attn_max_splits * kv_mul * kDecodePartStride * 4,
+                            (size_t)c.hidden * 4,
+                            G * 2 * 4,
+                            G * 4,
+                            kv,
+                            kv,
+                            (size_t)c.vocab * 4,
+                            4,
+                            4,
+                            (size_t)(c.max_seq + 1) * 4};
+    constexpr int kN = sizeof(sizes) / sizeof(sizes[0]);
     size_t total = 0;
     for (size_t b : sizes) total += al(b);
     cudaError_t e = cudaMalloc(&s->mem, total);
@@ -785,27 +846,26 @@ extern "C" int lc_session_create(lc_model* m, lc_session** out) {
         delete s;
         return cuda_fail(e, "session buffers");
     }
+    void* ptr[kN];
     uint8_t* p = (uint8_t*)s->mem;
-    void* ptrs[15];
-    for (int i = 0; i < 15; ++i) {
-        ptrs[i] = p;
+    for (int i = 0; i < kN; ++i) {
+        ptr[i] = p;
         p += al(sizes[i]);
     }
-    s->kcache = (float*)ptrs[0];
-    s->vcache = (float*)ptrs[1];
-    s->x = (float*)ptrs[2];
-    s->qbuf = (float*)ptrs[3];
-    s->att = (float*)ptrs[4];
-    s->hbuf = (float*)ptrs[5];
-    s->logits = (float*)ptrs[6];
-    s->attn_part = (float*)ptrs[7];
-    s->amax_val = (float*)ptrs[8];
-    s->attn_cnt = (uint32_t*)ptrs[9];
-    s->bar = (uint32_t*)ptrs[10];
-    s->amax_idx = (int*)ptrs[11];
-    s->err = (int*)ptrs[12];
-    s->n_done = (int*)ptrs[13];
-    s->tokens = (int32_t*)ptrs[14];
+    s->xa = (float*)ptr[0];
+    s->xb = (float*)ptr[1];
+    s->q = (float*)ptr[2];
+    s->att = (float*)ptr[3];
+    s->part = (float*)ptr[4];
+    s->h = (float*)ptr[5];
+    s->amax = (float*)ptr[6];
+    s->flags = (uint32_t*)ptr[7];
+    s->kcache = (float*)ptr[8];
+    s->vcache = (float*)ptr[9];
+    s->logits = (float*)ptr[10];
+    s->err = (int*)ptr[11];
+    s->n_done = (int*)ptr[12];
+    s->tokens = (int32_t*)ptr[13];
     e = cudaMemset(s->mem, 0, total);
     if (e == cudaSuccess) e = cudaMallocHost((void**)&s->pinned, (size_t)(c.max_seq + 8) * 4);
     if (e == cudaSuccess) e = cudaEventCreate(&s->ev0);
@@ -826,6 +886,7 @@ extern "C" int lc_session_destroy(lc_session* s) {
     if (s->pinned) cudaFreeHost(s->pinned);
     if (s->ev0) cudaEventDestroy(s->ev0);
     if (s->ev1) cudaEventDestroy(s->ev1);
+    if (s->trace) cudaFree(s->trace);
     delete s;
     return LC_OK;
 }
@@ -839,19 +900,21 @@ static int run_steps(lc_session* s, int pos0, int nsteps, int n_prompt, int skip
     fill_model_params(m, &p);
     p.kcache = s->kcache;
     p.vcache = s->vcache;
-    p.x = s->x;
-    p.qbuf = s->qbuf;
-    p.att = s->att;
-    p.hbuf = s->hbuf;
     p.logits = s->logits;
-    p.attn_part = s->attn_part;
-    p.attn_cnt = s->attn_cnt;
-    p.amax_val = s->amax_val;
-    p.amax_idx = s->amax_idx;
     p.tokens = s->tokens;
-    p.bar = s->bar;
     p.err = s->err;
     p.n_done = s->n_done;
+    p.xa = s->xa;
+    p.xb = s->xb;
+    p.q = s->q;
+    p.att = s->att;
+    p.part = s->part;
+    p.h = s->h;
+    p.amax = s->amax;
+    p.flags = s->flags;
+    // Exchange tags count up from 1 within a launch; the flags start at 0.
+    CK(cudaMemsetAsync(s->flags, 0, (size_t)m->launch.grid * 4, st), "clear exchange flags");
+    p.tag_base = 0;
     p.pos0 = pos0;
     p.nsteps = nsteps;
     p.n_prompt = n_prompt;
@@ -859,8 +922,11 @@ static int run_steps(lc_session* s, int pos0, int nsteps, int n_prompt, int skip
     p.n_stop = n_stop;
     for (int i = 0; i < n_stop; ++i) p.stop[i] = stop[i];
     p.attn_max_splits = s->attn_max_splits;
+    p.trace = s->trace;
+    p.trace_words = s->trace_words;
+    if (s->trace)
+        CK(cudaMemsetAsync(s->trace, 0, (size_t)m->launch.grid * s->trace_words * 8, st), "clear trace");
     CK(cudaMemsetAsync(s->err, 0, sizeof(int), st), "clear error word");
-    CK(cudaMemsetAsync(s->attn_cnt, 0, (size_t)m->cfg.n_kv_heads * 4, st), "clear attention counters");
     CK(cudaEventRecord(s->ev0, st), "event");
     CK(launch_decode(p, m->launch, st), "decode kernel launch");
     CK(cudaEventRecord(s->ev1, st), "event");
@@ -936,6 +1002,32 @@ extern "C" int lc_decode(lc_session* s, int32_t token, int32_t start_pos, int32_
     if (rc) return rc;
     CK(cudaMemcpyAsync(out_tokens, s->tokens + start_pos + 1, (size_t)n_steps * 4, cudaMemcpyDefault, st), "tokens copy");
     CK(cudaStreamSynchronize(st), "decode");
+    return LC_OK;
+}
+
+extern "C" int lc_session_enable_trace(lc_session* s, int32_t words_per_cta) {
+    if (!s || words_per_cta < 0) return fail(LC_ERR_INVALID_ARG, "bad argument");
+    CTX_CHECK(s->m->ctx);
+    CK(cudaStreamSynchronize(s->m->ctx->stream), "synchronize");
+    if (s->trace) cudaFree(s->trace);
+    s->trace = nullptr;
+    s->trace_words = 0;
+    if (words_per_cta == 0) return LC_OK;
+    CK(cudaMalloc(&s->trace, (size_t)s->m->launch.grid * words_per_cta * 8), "trace buffer");
+    s->trace_words = words_per_cta;
+    return LC_OK;
+}
+
+extern "C" int lc_session_read_trace(lc_session* s, uint64_t* out, int64_t n_words, int32_t* grid,
+                                     int32_t* words_per_cta) {
+    if (!s) return fail(LC_ERR_INVALID_ARG, "session is NULL");
+    CTX_CHECK(s->m->ctx);
+    if (grid) *grid = s->m->launch.grid;
+    if (words_per_cta) *words_per_cta = s->trace_words;
+    if (!out || !s->trace) return LC_OK;
+    const int64_t total = (int64_t)s->m->launch.grid * s->trace_words;
+    CK(cudaMemcpy(out, s->trace, (size_t)(n_words < total ? n_words : total) * 8, cudaMemcpyDeviceToHost),
+       "trace copy");
     return LC_OK;
 }
 

@@ -29,10 +29,14 @@ __host__ __device__ inline int attn_unit_smem_floats(int kv_mul, int tmax) {
 // Partial record per (split, head): [m, l, o[64]].
 constexpr int kAttnPartStride = kAttnHeadDim + 2;
 
-__device__ __forceinline__ void attention_unit(const float* __restrict__ q, const float* __restrict__ K,
+// Scores, softmax and weighted values of one unit.  nsplit == 1 writes the
+// normalised output of the kv_mul heads to out[h * 64 + i]; otherwise the
+// partial record of (split, h) goes to part[(split * kv_mul + h) * stride].
+// Ends with the unit's stores issued (no barrier after them).
+__device__ __forceinline__ void attention_core(const float* __restrict__ q, const float* __restrict__ K,
                                                const float* __restrict__ Vc, int64_t pos_stride, int t0, int t1,
                                                int nsplit, int split, float* __restrict__ out,
-                                               float* __restrict__ part, uint32_t* cnt, float scale, int kv_mul,
+                                               float* __restrict__ part, int part_stride, float scale, int kv_mul,
                                                int tmax, float* sm) {
     constexpr int HD = kAttnHeadDim;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -40,7 +44,6 @@ __device__ __forceinline__ void attention_unit(const float* __restrict__ q, cons
     float* qs = sm;
     float* sc = qs + kv_mul * HD;
     float* st = sc + kv_mul * tmax;
-    volatile int* flag = reinterpret_cast<volatile int*>(st + 2 * kv_mul);
 
     for (int i = tid; i < kv_mul * HD; i += 256) qs[i] = __ldcg(q + i);
     named_bar_sync(1, 256);
@@ -69,7 +72,7 @@ __device__ __forceinline__ void attention_unit(const float* __restrict__ q, cons
         float m = -INFINITY;
         for (int t = lane; t < T; t += 32) m = fmaxf(m, e[t]);
         m = warp_max(m);
-        for (int t = lane; t < T; t += 32) e[t] = exp_via_double(__fsub_rn(e[t], m));
+        for (int t = lane; t < T; t += 32) e[t] = exp_via_double_nl(__fsub_rn(e[t], m));
         __syncwarp();
         float l = 0.0f;
         if (nsplit == 1) {
@@ -102,7 +105,7 @@ __device__ __forceinline__ void attention_unit(const float* __restrict__ q, cons
         } else {
 #pragma unroll 4
             for (int t = 0; t < T; ++t) acc = fmaf(e[t], __ldcg(vcol + (int64_t)t * pos_stride), acc);
-            float* pp = part + ((int64_t)split * kv_mul + h) * kAttnPartStride;
+            float* pp = part + ((int64_t)split * kv_mul + h) * part_stride;
             pp[2 + i] = acc;
             if (i == 0) {
                 pp[0] = st[2 * h];
@@ -110,7 +113,19 @@ __device__ __forceinline__ void attention_unit(const float* __restrict__ q, cons
             }
         }
     }
+}
 
+// Standalone unit: attention_core, then with several splits the last unit to
+// finish (ticket on *cnt) merges the partials into out.
+__device__ __forceinline__ void attention_unit(const float* __restrict__ q, const float* __restrict__ K,
+                                               const float* __restrict__ Vc, int64_t pos_stride, int t0, int t1,
+                                               int nsplit, int split, float* __restrict__ out,
+                                               float* __restrict__ part, uint32_t* cnt, float scale, int kv_mul,
+                                               int tmax, float* sm) {
+    constexpr int HD = kAttnHeadDim;
+    const int tid = threadIdx.x;
+    attention_core(q, K, Vc, pos_stride, t0, t1, nsplit, split, out, part, kAttnPartStride, scale, kv_mul, tmax, sm);
+    volatile int* flag = reinterpret_cast<volatile int*>(sm + kv_mul * HD + kv_mul * tmax + 2 * kv_mul);
     if (nsplit > 1) {
         __threadfence();
         named_bar_sync(1, 256);

@@ -102,6 +102,12 @@ LC_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, 
         : "memory");
 }
 
+// Starts pulling [src, src+bytes) from HBM into L2 without waiting for it
+// (no shared-memory destination, no completion tracking).  bytes % 16 == 0.
+LC_DEV void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // ------------------------------------------------------ named CTA barriers --
 
 LC_DEV void named_bar_sync(uint32_t id, uint32_t nthreads) {
@@ -115,6 +121,8 @@ LC_DEV uint32_t ld_acquire_gpu(const uint32_t* p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+
+LC_DEV void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
 LC_DEV void red_release_gpu_add(uint32_t* p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -140,6 +148,17 @@ LC_DEV float exp_via_double(float x) { return static_cast<float>(exp(static_cast
 // x / (1.0f + (float)Math.exp(-x))  (SiLU.java:36-39), no contraction.
 LC_DEV float silu_ref(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, exp_via_double(-x))); }
 
+// Out-of-line copies for the fused kernel: one body each instead of one per
+// call site keeps its instruction footprint small.
+static __device__ __noinline__ float exp_via_double_nl(float x) { return exp_via_double(x); }
+static __device__ __noinline__ float silu_ref_nl(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, exp_via_double(-x))); }
+// (float)Math.cos / Math.sin of (double)val (RoPE.java:45-46).
+static __device__ __noinline__ float2 sincos_ref_nl(float val) {
+    double s, c;
+    sincos((double)val, &s, &c);
+    return make_float2((float)s, (float)c);
+}
+
 // 8 packed halves -> 8 floats.
 LC_DEV void unpack_h8(const uint4& w, float f[8]) {
     const __half2* h = reinterpret_cast<const __half2*>(&w);
@@ -160,6 +179,34 @@ LC_DEV void argmax_merge(float& bv, int& bi, float v, int i) {
         bv = v;
         bi = i;
     }
+}
+
+}  // namespace lc
+
+
+namespace lc {
+
+// ------------------------------------------------------ exchange flags --
+LC_DEV void st_flag(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+LC_DEV uint32_t ld_flag(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// CTA-uniform OR of a predicate over the threads of named barrier `id`.
+LC_DEV bool bar_red_or(uint32_t id, uint32_t nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
 }
 
 }  // namespace lc

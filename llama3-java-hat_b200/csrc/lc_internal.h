@@ -54,43 +54,65 @@ cudaError_t launch_attention_decode(const AttnPlan& p, const float* q, const flo
                                     int64_t pos_stride, void* scratch, cudaStream_t st);
 
 // ---- fused decode step (lc_decode.cu) ----
+//
+// GEMV weights of the fused kernel live in HBM as row-group tiles: a tile is
+// 8 consecutive rows x CB = dim consecutive columns, stored as
+// [CB / 8 column octets][8 rows][8 halves] (16 * CB bytes, contiguous), and
+// tile (g, cb) of a matrix with ncb = cols / CB column blocks starts at
+// element (g * ncb + cb) * 8 * CB.  One 1-D bulk copy moves a tile into
+// shared memory, where the 8x8 half blocks feed ldmatrix without bank
+// conflicts.  Rows are padded to a multiple of 8 with zeros.
 struct LayerW {
-    const __half* wqkv;   // [dim + 2*kv_dim][dim]
-    const __half* wo;     // [dim][n_heads*head_dim]
-    const __half* wgu;    // [2*hidden][dim], row 2r = gate r, row 2r+1 = up r
-    const __half* wdown;  // [dim][hidden]
+    const __half* wqkv;   // tiled [dim + 2*kv_dim][dim]
+    const __half* wo;     // tiled [dim][n_heads*head_dim]
+    const __half* wgu;    // tiled [2*hidden][dim], row 2r = gate r, row 2r+1 = up r
+    const __half* wdown;  // tiled [dim][hidden]
     const float* attn_norm;
     const float* ffn_norm;
 };
 
+// Element offset of (row, col) in the tiled layout of a matrix with `cols`
+// columns and column-block width cb.
+__host__ __device__ inline size_t tiled_offset(int64_t row, int64_t col, int64_t cols, int64_t cb) {
+    const int64_t ncb = cols / cb;
+    return (size_t)((((row >> 3) * ncb + col / cb) * 8 * cb) + ((col % cb) >> 3) * 64 + (row & 7) * 8 + (col & 7));
+}
+
+// Rewrites a row-major F16 matrix [rows][cols] into the tiled layout:
+// source row r becomes row row0 + r * row_step of the destination matrix.
+cudaError_t launch_tile_rows(const __half* src, __half* dst, int rows, int cols, int cb, int row0, int row_step,
+                             cudaStream_t st);
+
 constexpr int kMaxStop = 32;
+constexpr int kDecodePartStride = 68;  // floats per attention partial: m, l, o[64], pad
 
 struct DecodeParams {
     // model
     int dim, hidden, n_layers, n_heads, n_kv, head_dim, vocab, max_seq;
     float eps;
     float attn_scale;
-    const __half* tok_emb;
-    const __half* lm_head;
+    const __half* tok_emb;  // row-major [vocab][dim]
+    const __half* lm_head;  // tiled [vocab rounded up to 8][dim]
     const float* out_norm;
-    const LayerW* layers;  // device array [n_layers]
+    const LayerW* layers;   // device array [n_layers]
     RopeFreq rope;
     // session buffers (device)
     float* kcache;  // [n_layers][n_kv][max_seq][head_dim]
     float* vcache;
-    float* x;       // [dim]
-    float* qbuf;    // [n_heads*head_dim]
-    float* att;     // [n_heads*head_dim]
-    float* hbuf;    // [hidden]
     float* logits;  // [vocab]
-    float* attn_part;      // attention partials
-    uint32_t* attn_cnt;    // [n_kv] completion counters, self-resetting
-    float* amax_val;       // [grid]
-    int* amax_idx;         // [grid]
     int32_t* tokens;       // [max_seq + 1]: token fed at each position
-    uint32_t* bar;         // grid barrier counter, zero at launch
     int* err;              // device error word
     int* n_done;           // steps completed
+    // Exchange buffers, published through per-CTA flags.
+    float* xa;             // [dim]   x after the attention residual
+    float* xb;             // [dim]   x after the FFN residual
+    float* q;              // [n_heads*head_dim] rotated q of the current position
+    float* att;            // [n_heads*head_dim] attention output (single split)
+    float* part;           // [n_kv][attn_max_splits][kv_mul][kDecodePartStride] partials
+    float* h;              // [hidden] silu(gate)*up
+    float* amax;           // [grid][2] per-CTA argmax candidate (value, index bits)
+    uint32_t* flags;       // [grid] latest exchange tag each CTA has published
+    uint32_t tag_base;     // launch epoch << 20; tags are tag_base + exchange + 1
     // launch
     int pos0, nsteps, n_prompt;
     int skip_prefill_logits;
@@ -98,13 +120,25 @@ struct DecodeParams {
     int32_t stop[kMaxStop];
     int attn_max_splits;   // splits per kv head upper bound (partials layout)
     unsigned long long timeout_ns;
+    // Phase trace (debug): when non-null, consumer thread 0 of each CTA writes
+    // %globaltimer stamps into trace[cta*trace_words + k].
+    unsigned long long* trace;
+    int trace_words;
+    // Producer L2 prefetch distance, in tiles beyond the tile being copied
+    // into shared memory (0 = no L2 prefetch).
+    int l2_prefetch_stages;
 };
 
 struct DecodeLaunch {
     int grid;
     int smem_bytes;
-    int seg_vec;  // V: 256*V columns per segment
+    int ks;      // k-steps of 16 columns per consumer warp: dim / 128
+    int stages;  // ring stages
 };
+
+// Splits per kv head the attention phase can use up to max_seq (partials
+// layout of DecodeParams::part).
+int decode_attn_max_splits(int max_seq, int grid, int n_kv);
 
 // Validates the configuration against what the fused kernel implements and
 // fills the launch shape.  Returns false with a message when unsupported.

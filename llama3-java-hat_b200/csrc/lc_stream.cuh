@@ -136,36 +136,59 @@ struct Consumer {
     // Dots rows [r0, r1) of a job (cols = nseg*S) with the warp's activation
     // slice xr; the per-(row, segment) partial of warp-reduced fp32 sums goes
     // to ys[(row - r0) * nseg + seg].  Returns false on timeout / error.
+    uint64_t wait_ns = 0;  // time spent waiting for stages (diagnostics, thread 0)
+    bool timing = false;
+
     template <int V>
     __device__ __forceinline__ bool consume_rows(const Ring& ring, int nseg, int r0, int r1, const float (&xr)[8 * V],
                                                  float* ys, volatile int* err, uint64_t timeout_ns) {
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
         const int srows = 8 / nseg;
         const int my_row = warp / nseg, my_seg = warp % nseg;
+        uint32_t slot = it % kStages, par = (it / kStages) & 1u;
+        // Compact loop body (one stage per iteration, nothing unrolled across
+        // stages): the decode kernel holds five copies of it and instruction
+        // fetch, not arithmetic, is what a bigger body costs.
+#pragma unroll 1
         for (int r = r0; r < r1; r += srows) {
-            const int n = min(srows, r1 - r);
-            const uint32_t slot = it % kStages;
-            const uint32_t par = (it / kStages) & 1u;
-            if (!mbar_wait_bounded(&ring.full[slot], par, err, globaltimer_ns() + timeout_ns, kDevTimeoutFull))
+            if (timing) {
+                const uint64_t t0 = globaltimer_ns();
+                if (!mbar_wait_bounded(&ring.full[slot], par, err, t0 + timeout_ns, kDevTimeoutFull)) return false;
+                wait_ns += globaltimer_ns() - t0;
+            } else if (!mbar_try_wait(&ring.full[slot], par) &&
+                       !mbar_wait_bounded(&ring.full[slot], par, err, globaltimer_ns() + timeout_ns, kDevTimeoutFull)) {
                 return false;
-            if (my_row < n) {
+            }
+            if (r + my_row < r1) {
                 const uint8_t* base = ring.buf + (size_t)slot * Geo<V>::kStageBytes +
                                       (size_t)(my_row * nseg + my_seg) * Geo<V>::kSegBytes + (size_t)lane * 16;
-                float acc = 0.0f;
+                uint4 wv[V];
+#pragma unroll
+                for (int v = 0; v < V; ++v) wv[v] = *reinterpret_cast<const uint4*>(base + v * 512);
+                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
 #pragma unroll
                 for (int v = 0; v < V; ++v) {
-                    const uint4 wv = *reinterpret_cast<const uint4*>(base + v * 512);
-                    float f[8];
-                    unpack_h8(wv, f);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) acc = fmaf(f[j], xr[v * 8 + j], acc);
+                    const __half2* h2 = reinterpret_cast<const __half2*>(&wv[v]);
+                    const float2 t0 = __half22float2(h2[0]), t1 = __half22float2(h2[1]);
+                    const float2 t2 = __half22float2(h2[2]), t3 = __half22float2(h2[3]);
+                    a0 = fmaf(t0.y, xr[v * 8 + 1], fmaf(t0.x, xr[v * 8 + 0], a0));
+                    a1 = fmaf(t1.y, xr[v * 8 + 3], fmaf(t1.x, xr[v * 8 + 2], a1));
+                    a2 = fmaf(t2.y, xr[v * 8 + 5], fmaf(t2.x, xr[v * 8 + 4], a2));
+                    a3 = fmaf(t3.y, xr[v * 8 + 7], fmaf(t3.x, xr[v * 8 + 6], a3));
                 }
-                acc = warp_sum(acc);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ring.empty[slot]);  // weights are in registers now
+                float acc = warp_sum((a0 + a1) + (a2 + a3));
                 if (lane == 0) ys[(r - r0 + my_row) * nseg + my_seg] = acc;
+            } else {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ring.empty[slot]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ring.empty[slot]);
             ++it;
+            if (++slot == (uint32_t)kStages) {
+                slot = 0;
+                par ^= 1u;
+            }
         }
         return true;
     }

@@ -107,6 +107,8 @@ SIGNATURES = {
     "lc_forward": (c_int, [c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
     "lc_generate": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int32, c_void_p, c_void_p]),
     "lc_decode": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_void_p]),
+    "lc_session_enable_trace": (c_int, [c_void_p, c_int32]),
+    "lc_session_read_trace": (c_int, [c_void_p, c_void_p, c_int64, POINTER(c_int32), POINTER(c_int32)]),
     "lc_session_last_ms": (c_int, [c_void_p, POINTER(c_float)]),
 }
 

@@ -97,6 +97,20 @@ class Session:
         _lib.check(lib.lc_decode(self.handle, int(token), int(start_pos), int(n_steps), _addr(o, "i32", n_steps, True)))
         return o
 
+    def enable_trace(self, words_per_cta: int) -> None:
+        """Phase trace of the fused kernel (see lc_session_enable_trace)."""
+        _lib.check(_lib.load().lc_session_enable_trace(self.handle, int(words_per_cta)))
+
+    def read_trace(self) -> np.ndarray:
+        """[grid][words_per_cta] uint64 %globaltimer stamps (0 = not written)."""
+        lib = _lib.load()
+        g, w = ctypes.c_int32(), ctypes.c_int32()
+        _lib.check(lib.lc_session_read_trace(self.handle, None, 0, ctypes.byref(g), ctypes.byref(w)))
+        out = np.zeros((g.value, w.value), np.uint64)
+        if out.size:
+            _lib.check(lib.lc_session_read_trace(self.handle, out.ctypes.data, out.size, None, None))
+        return out
+
     def last_ms(self) -> float:
         v = ctypes.c_float()
         _lib.check(_lib.load().lc_session_last_ms(self.handle, ctypes.byref(v)))

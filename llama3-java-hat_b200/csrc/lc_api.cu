@@ -508,7 +508,9 @@ struct lc_model {
     bool finalized = false;
     RopeFreq rope;
     DecodeLaunch launch;
-    int l2_prefetch_stages = 0;  // producer L2 prefetch distance (tiles)
+    uint32_t* d_sched = nullptr;  // producer tile schedule (decode_build_schedule)
+    int* d_sched_n = nullptr;
+    int sched_stride = 0;
 };
 
 static int validate_config(const lc_config* c) {
@@ -588,6 +590,8 @@ extern "C" int lc_model_destroy(lc_model* m) {
     if (m->arena) cudaFree(m->arena);
     if (m->staging) cudaFree(m->staging);
     if (m->d_layers) cudaFree(m->d_layers);
+    if (m->d_sched) cudaFree(m->d_sched);
+    if (m->d_sched_n) cudaFree(m->d_sched_n);
     delete m;
     return LC_OK;
 }
@@ -754,7 +758,10 @@ static void fill_model_params(const lc_model* m, DecodeParams* p) {
     p->layers = m->d_layers;
     p->rope = m->rope;
     p->timeout_ns = 2000000000ull;
-    p->l2_prefetch_stages = m->l2_prefetch_stages;
+    p->sched = m->d_sched;
+    p->sched_n = m->d_sched_n;
+    p->sched_stride = m->sched_stride;
+    p->wbase = (const uint8_t*)m->arena;
 }
 
 extern "C" int lc_model_finalize(lc_model* m) {
@@ -776,7 +783,6 @@ extern "C" int lc_model_finalize(lc_model* m) {
     m->staging = nullptr;
     m->staging_bytes = 0;
     make_rope_freq(&m->rope, m->cfg.rope_theta, m->cfg.head_dim);
-    if (const char* e = getenv("LLAMACUDA_L2_PREFETCH_STAGES")) m->l2_prefetch_stages = atoi(e);
     std::vector<LayerW> lw(m->cfg.n_layers);
     for (int l = 0; l < m->cfg.n_layers; ++l) {
         const LayerStore& L = m->layers[l];
@@ -788,7 +794,17 @@ extern "C" int lc_model_finalize(lc_model* m) {
     fill_model_params(m, &p);
     const char* why = nullptr;
     if (!decode_plan(p, m->ctx->sms, &m->launch, &why)) return fail(LC_ERR_UNSUPPORTED, "%s", why);
+    {
+        std::vector<uint32_t> sched;
+        std::vector<int> counts;
+        decode_build_schedule(p, lw.data(), m->launch.grid, &sched, &counts, &m->sched_stride);
+        CK(cudaMalloc(&m->d_sched, sched.size() * 4), "tile schedule");
+        CK(cudaMalloc(&m->d_sched_n, counts.size() * 4), "tile schedule");
+        CK(cudaMemcpy(m->d_sched, sched.data(), sched.size() * 4, cudaMemcpyHostToDevice), "tile schedule");
+        CK(cudaMemcpy(m->d_sched_n, counts.data(), counts.size() * 4, cudaMemcpyHostToDevice), "tile schedule");
+    }
     CK(decode_prepare(m->launch), "decode kernel setup");
+    CK(decode_prepare_traced(m->launch), "decode kernel setup");
     m->finalized = true;
     return LC_OK;
 }
@@ -798,7 +814,10 @@ extern "C" int lc_model_finalize(lc_model* m) {
 struct lc_session {
     lc_model* m = nullptr;
     void* mem = nullptr;
-    float *xa, *xb, *q, *att, *part, *h, *amax;
+    size_t tagged_bytes = 0;  // the tagged exchange words at the start of mem
+    uint64_t *xa, *xb, *q, *kv, *att, *part, *amax;
+    float* h;
+    uint32_t epoch = 0;       // launch counter: tags of launch e are e << 20 | exchange
     uint32_t* flags;
     float *kcache, *vcache, *logits;
     int *err, *n_done;
@@ -822,15 +841,17 @@ extern "C" int lc_session_create(lc_model* m, lc_session** out) {
     s->attn_max_splits = decode_attn_max_splits(c.max_seq, m->launch.grid, c.n_kv_heads);
     const size_t G = (size_t)m->launch.grid;
     auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
-    const size_t qd = (size_t)c.n_heads * c.head_dim;
+    const size_t qd = (size_t)c.n_heads * c.head_dim, kvd = (size_t)c.n_kv_heads * c.head_dim;
     const size_t kv = (size_t)c.n_layers * c.n_kv_heads * c.max_seq * c.head_dim * 4;
-    const size_t sizes[] = {(size_t)c.dim * 4,
-                            (size_t)c.dim * 4,
-                            qd * 4,
-                            qd * 4,
-                            (size_t)c.n_kv_heads * s->attn_max_splits * kv_mul * kDecodePartStride * 4,
+    // Tagged exchange words (8 bytes each) first, then plain buffers.
+    const size_t sizes[] = {(size_t)c.dim * 8,
+                            (size_t)c.dim * 8,
+                            qd * 8,
+                            2 * kvd * 8,
+                            qd * 8,
+                            (size_t)c.n_kv_heads * s->attn_max_splits * kv_mul * kDecodePartStride * 8,
+                            G * 2 * 8,
                             (size_t)c.hidden * 4,
-                            G * 2 * 4,
                             G * 4,
                             kv,
                             kv,
@@ -852,20 +873,22 @@ extern "C" int lc_session_create(lc_model* m, lc_session** out) {
         ptr[i] = p;
         p += al(sizes[i]);
     }
-    s->xa = (float*)ptr[0];
-    s->xb = (float*)ptr[1];
-    s->q = (float*)ptr[2];
-    s->att = (float*)ptr[3];
-    s->part = (float*)ptr[4];
-    s->h = (float*)ptr[5];
-    s->amax = (float*)ptr[6];
-    s->flags = (uint32_t*)ptr[7];
-    s->kcache = (float*)ptr[8];
-    s->vcache = (float*)ptr[9];
-    s->logits = (float*)ptr[10];
-    s->err = (int*)ptr[11];
-    s->n_done = (int*)ptr[12];
-    s->tokens = (int32_t*)ptr[13];
+    s->xa = (uint64_t*)ptr[0];
+    s->xb = (uint64_t*)ptr[1];
+    s->q = (uint64_t*)ptr[2];
+    s->kv = (uint64_t*)ptr[3];
+    s->att = (uint64_t*)ptr[4];
+    s->part = (uint64_t*)ptr[5];
+    s->amax = (uint64_t*)ptr[6];
+    s->tagged_bytes = (size_t)((uint8_t*)ptr[7] - (uint8_t*)ptr[0]);
+    s->h = (float*)ptr[7];
+    s->flags = (uint32_t*)ptr[8];
+    s->kcache = (float*)ptr[9];
+    s->vcache = (float*)ptr[10];
+    s->logits = (float*)ptr[11];
+    s->err = (int*)ptr[12];
+    s->n_done = (int*)ptr[13];
+    s->tokens = (int32_t*)ptr[14];
     e = cudaMemset(s->mem, 0, total);
     if (e == cudaSuccess) e = cudaMallocHost((void**)&s->pinned, (size_t)(c.max_seq + 8) * 4);
     if (e == cudaSuccess) e = cudaEventCreate(&s->ev0);
@@ -907,14 +930,24 @@ static int run_steps(lc_session* s, int pos0, int nsteps, int n_prompt, int skip
     p.xa = s->xa;
     p.xb = s->xb;
     p.q = s->q;
+    p.kv = s->kv;
     p.att = s->att;
     p.part = s->part;
     p.h = s->h;
     p.amax = s->amax;
     p.flags = s->flags;
-    // Exchange tags count up from 1 within a launch; the flags start at 0.
+    // Exchange indices of one launch must fit the 20 low bits of a tag.
+    if ((int64_t)nsteps * (5 * m->cfg.n_layers + 1) >= (int64_t)(1 << 20) - 1)
+        return fail(LC_ERR_UNSUPPORTED, "%d steps in one launch exceed the exchange-tag range", nsteps);
+    // Tags are epoch << 20 | exchange + 1: words left by earlier launches never
+    // match.  When the 12-bit epoch wraps, the words are cleared.  The flags
+    // restart from 0 every launch.
+    if (++s->epoch >= 4096u) {
+        CK(cudaMemsetAsync(s->mem, 0, s->tagged_bytes, st), "clear exchange words");
+        s->epoch = 1;
+    }
     CK(cudaMemsetAsync(s->flags, 0, (size_t)m->launch.grid * 4, st), "clear exchange flags");
-    p.tag_base = 0;
+    p.tag_base = s->epoch << 20;
     p.pos0 = pos0;
     p.nsteps = nsteps;
     p.n_prompt = n_prompt;
@@ -928,7 +961,7 @@ static int run_steps(lc_session* s, int pos0, int nsteps, int n_prompt, int skip
         CK(cudaMemsetAsync(s->trace, 0, (size_t)m->launch.grid * s->trace_words * 8, st), "clear trace");
     CK(cudaMemsetAsync(s->err, 0, sizeof(int), st), "clear error word");
     CK(cudaEventRecord(s->ev0, st), "event");
-    CK(launch_decode(p, m->launch, st), "decode kernel launch");
+    CK(s->trace ? launch_decode_traced(p, m->launch, st) : launch_decode(p, m->launch, st), "decode kernel launch");
     CK(cudaEventRecord(s->ev1, st), "event");
     CK(cudaMemcpyAsync(s->pinned, s->err, 4, cudaMemcpyDeviceToHost, st), "read error word");
     CK(cudaMemcpyAsync(s->pinned + 1, s->n_done, 4, cudaMemcpyDeviceToHost, st), "read step count");

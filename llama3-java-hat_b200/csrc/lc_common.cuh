@@ -186,6 +186,44 @@ LC_DEV void argmax_merge(float& bv, int& bi, float v, int i) {
 
 namespace lc {
 
+// ------------------------------------------------- tagged exchange words --
+//
+// Exchanged activations travel as 64-bit words: the float's bits in the low
+// half, the tag of the exchange that produced them in the high half.  An
+// aligned 64-bit store is single-copy atomic, so a reader that sees the tag
+// it waits for also sees the value stored with it, without a fence on
+// either side.
+
+LC_DEV uint64_t tag_word(float v, uint32_t tag) { return ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v); }
+
+// Two tagged words, 16 bytes, p 16-byte aligned.
+LC_DEV void st_tag2(uint64_t* p, float a, float b, uint32_t tag) {
+    asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(tag_word(a, tag)), "l"(tag_word(b, tag))
+                 : "memory");
+}
+LC_DEV void st_tag1(uint64_t* p, float a, uint32_t tag) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(tag_word(a, tag)) : "memory");
+}
+LC_DEV void ld_word2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+// Four tagged words at p (16-byte aligned) -> v; true when all carry `want`.
+LC_DEV bool ld_tag4(const uint64_t* p, uint32_t want, float4& v) {
+    uint64_t a, b, c, d;
+    ld_word2(p, a, b);
+    ld_word2(p + 2, c, d);
+    v = make_float4(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)b), __uint_as_float((uint32_t)c),
+                    __uint_as_float((uint32_t)d));
+    return (uint32_t)(a >> 32) == want && (uint32_t)(b >> 32) == want && (uint32_t)(c >> 32) == want &&
+           (uint32_t)(d >> 32) == want;
+}
+LC_DEV bool ld_tag2(const uint64_t* p, uint32_t want, float2& v) {
+    uint64_t a, b;
+    ld_word2(p, a, b);
+    v = make_float2(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)b));
+    return (uint32_t)(a >> 32) == want && (uint32_t)(b >> 32) == want;
+}
+
 // ------------------------------------------------------ exchange flags --
 LC_DEV void st_flag(uint32_t* p, uint32_t v) {
     asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");

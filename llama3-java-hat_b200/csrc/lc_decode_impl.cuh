@@ -1,0 +1,1343 @@
+// lc_decode.cu -- the fused decode step: LlamaInference.forward
+// (LlamaInference.java:117-164) with all TransformerBlock.forward calls
+// (TransformerBlock.java:130-217), the final RMSNorm, the lm_head GEMV and the
+// greedy argmax, for `nsteps` consecutive positions, in ONE cooperative
+// persistent launch (one CTA per SM).
+//
+// Jobs of one position, in order, each ending with an exchange:
+//   QKV  rmsnorm(x, attn_norm) -> [Wq;Wk;Wv] GEMV -> RoPE(q,k) -> q, KV cache
+//   ATT  GQA attention units (kv head x split of positions) -> att / partials
+//   O    (combine partials) -> Wo GEMV + residual -> x
+//   GU   rmsnorm(x, ffn_norm) -> [gate|up] GEMV -> silu(gate)*up -> h
+//   DN   Wdown GEMV + residual -> x
+//   LM   rmsnorm(x, out_norm) -> lm_head GEMV -> logits, per-CTA argmax;
+//        every CTA then merges the candidates into the next token.
+//
+// Weight bytes are >99.8% of the traffic.  One producer thread per CTA walks
+// the CTA's whole multi-step tile schedule and moves 8-row weight tiles
+// (layout in lc_internal.h) into a ring of shared-memory stages with 1-D bulk
+// copies; it never waits for activations, so HBM keeps streaming while the
+// consumer warps exchange data with the other CTAs.  Eight consumer warps
+// each own a fixed column slice of every tile: the activation slice sits in
+// registers as f16 hi/lo pairs (x*2^e = hi + lo to 2^-22, exact products)
+// and the tile rows come in with ldmatrix, so a tile costs a warp a handful
+// of mma.sync m16n8k16 with fp32 accumulation.  Per-warp partial sums meet in
+// shared memory and the job epilogue adds them in a fixed order.
+//
+// Exchanges: a CTA raises its flag word to a monotonically increasing tag
+// after its stores for an exchange; a reader's warp 0 polls all flags, then
+// the CTA reads the data from L2.  Every wait is bounded: a timeout records an
+// error code in p.err, every later wait returns at once, all CTAs leave at
+// the next step boundary, the producer drains its in-flight copies, and the
+// host reports LC_ERR_TIMEOUT.
+#pragma once
+// Included by lc_decode.cu (LC_DECODE_TRACE 0) and lc_decode_trace.cu
+// (LC_DECODE_TRACE 1, the phase-trace build of the same kernel).
+#include "lc_attention.cuh"
+#include "lc_internal.h"
+#include "lc_stream.cuh"
+
+#ifndef LC_DECODE_TRACE
+#error "define LC_DECODE_TRACE before including lc_decode_impl.cuh"
+#endif
+
+namespace lc {
+
+namespace {
+
+constexpr int kCW = 8;                // consumer warps
+constexpr int kCT = kCW * 32;         // consumer threads
+constexpr int kThreads = kCT + 128;   // + one warpgroup: the producer thread (warp kCW) and idle warps
+// Register split (setmaxnreg, per warpgroup): the launch gives every thread
+// 65536 / kThreads -> 168 registers; the producer warpgroup gives most of its
+// share to the consumer warpgroups.  The sum must stay within the launch
+// total or setmaxnreg.inc would wait forever.
+constexpr int kRegLaunch = 168, kRegConsumer = 224, kRegProducer = 56;
+static_assert(kCT * kRegConsumer + 128 * kRegProducer <= kThreads * kRegLaunch, "register split exceeds the pool");
+constexpr uint32_t kBarC = 1;         // named barrier of the consumer threads
+constexpr int kBatchTiles = 8;        // tiles per epilogue batch
+constexpr int kMaxStages = 24;
+constexpr int kRingBytes = 192 * 1024;
+constexpr int kAttnTmin = 64;         // positions per attention unit, at least
+constexpr int kAttnTmax = 384;        // ... and at most
+constexpr int kVChunk = 64;           // V positions staged in shared memory at a time
+
+enum Kind : int { kQKV = 0, kO = 1, kGU = 2, kDN = 3, kLM = 4 };
+
+__host__ __device__ inline bool lm_needed(const DecodeParams& p, int pos) {
+    return !(p.skip_prefill_logits && pos + 1 < p.n_prompt);
+}
+
+// Positions per attention unit at sequence length `seq`: one unit per kv head
+// up to kAttnTmin positions (the exact single-split path), else about one
+// unit per CTA.
+__host__ __device__ inline int attn_split_len(int seq, int G, int n_kv) {
+    if (seq <= kAttnTmin) return seq;
+    int per = G / n_kv;
+    if (per < 1) per = 1;
+    int T = (seq + per - 1) / per;
+    if (T < kAttnTmin) T = kAttnTmin;
+    if (T > kAttnTmax) T = kAttnTmax;
+    return T;
+}
+
+// q, this position's k and v, K/V chunk, scores, per-head (max, sum).
+__host__ __device__ inline int attn_scratch_floats(int kv_mul) {
+    return kv_mul * (kAttnHeadDim + kAttnTmax) + 2 * kAttnHeadDim + kVChunk * kAttnHeadDim + 16;
+}
+
+struct Shared {
+    int stop;       // consumers -> producer: leave
+    int next;       // argmax broadcast
+    float unscale;  // 2^-e of the staged GEMV input (see stage_split)
+    int pad;
+    float red[kCW];
+    float rmax[kCW];
+    float bv[kCW];
+    int bi[kCW];
+};
+
+// Shared-memory layout for dim = 128 * KS (offsets in bytes from the
+// 1024-aligned base), all compile-time constants: act holds the largest GEMV
+// input (h, up to kActFloats floats) or the attention scratch.
+constexpr int kActFloats = 8192;
+struct Layout {
+    int tile_bytes, stages;
+    int off_bar, off_sh, off_act, off_ys, total;
+};
+
+__host__ __device__ constexpr Layout make_layout(int dim) {
+    return Layout{16 * dim,
+                  kRingBytes / (16 * dim) < kMaxStages ? kRingBytes / (16 * dim) : kMaxStages,
+                  (kRingBytes / (16 * dim) < kMaxStages ? kRingBytes / (16 * dim) : kMaxStages) * 16 * dim,
+                  0, 0, 0, 0};
+}
+
+__host__ __device__ constexpr Layout finish_layout(Layout L) {
+    L.off_sh = L.off_bar + 2 * kMaxStages * 8;
+    L.off_act = L.off_sh + (int)((sizeof(Shared) + 15) / 16 * 16);
+    L.off_ys = L.off_act + kActFloats * 4;
+    L.total = L.off_ys + kBatchTiles * 8 * kCW * 4;
+    return L;
+}
+
+template <int KS>
+struct LayoutOf {
+    static constexpr Layout L = finish_layout(make_layout(128 * KS));
+};
+
+struct Smem {
+    uint8_t* ring;
+    uint64_t* full;
+    uint64_t* empty;
+    Shared* sh;
+    float* act;   // GEMV input (normalised x, att, h); attention scratch
+    float* ys;    // [tile][row][warp] partial dot products of one batch
+    int stages, tile_bytes;
+};
+
+// ------------------------------------------------------------- schedule --
+
+struct JobGeo {
+    const __half* W;
+    int groups;  // row groups of 8
+    int ncb;     // column blocks of dim columns
+};
+
+// Geometry of job `kind` of layer l (W from the layer table `layers`).
+__host__ __device__ __forceinline__ JobGeo job_geo(const DecodeParams& p, const LayerW* layers, int kind, int l) {
+    const int qdim = p.n_heads * p.head_dim, kvd = p.n_kv * p.head_dim;
+    if (kind == kLM) return {p.lm_head, (p.vocab + 7) / 8, 1};
+    const LayerW& L = layers[l];
+    switch (kind) {
+        case kQKV: return {L.wqkv, (qdim + 2 * kvd) / 8, 1};
+        case kO: return {L.wo, p.dim / 8, qdim / p.dim};
+        case kGU: return {L.wgu, 2 * p.hidden / 8, 1};
+        default: return {L.wdown, p.dim / 8, p.hidden / p.dim};
+    }
+}
+
+// Groups of a batch: at most kBatchTiles tiles, column-block-major inside.
+__host__ __device__ __forceinline__ int batch_groups(int ncb) {
+    const int b = kBatchTiles / ncb;
+    return b < 1 ? 1 : b;
+}
+
+// ------------------------------------------------------------- producer --
+
+// The producer warp walks the CTA's tile list of one position (built on the
+// host, same order as the consumers' jobs) once per position.  The 32 lanes
+// hold the next 32 entries (and prefetch the 32 after); lane 0 waits for a
+// free stage and issues the copy.
+__device__ __forceinline__ void run_producer(const DecodeParams& p, const Smem& sm) {
+    const int lane = threadIdx.x & 31, cta = blockIdx.x;
+    volatile int* err = p.err;
+    volatile int* stop = &sm.sh->stop;
+    const uint64_t policy = l2_policy_evict_first();
+    const uint32_t tb = (uint32_t)sm.tile_bytes;
+    const uint32_t nst = (uint32_t)sm.stages;
+    const uint32_t* row = p.sched + (size_t)cta * p.sched_stride;
+    const int nlay = p.sched_n[2 * cta], ntot = nlay + p.sched_n[2 * cta + 1];
+    uint32_t it = 0, slot = 0, par = 1;
+    bool ok = true;
+    for (int s = 0; s < p.nsteps && ok; ++s) {
+        const int n = lm_needed(p, p.pos0 + s) ? ntot : nlay;
+        uint32_t cur = lane < ntot ? __ldg(row + lane) : 0u;
+        uint32_t nxt = 32 + lane < ntot ? __ldg(row + 32 + lane) : 0u;
+        for (int i = 0; i < n; ++i) {
+            if ((i & 31) == 0 && i > 0) {
+                cur = nxt;
+                nxt = i + 32 + lane < ntot ? __ldg(row + i + 32 + lane) : 0u;
+            }
+            const uint32_t e = __shfl_sync(0xffffffffu, cur, i & 31);
+            int fail = 0;
+            if (lane == 0) {
+                if (!mbar_try_wait(&sm.empty[slot], par)) {
+                    const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
+                    for (uint32_t k = 1;; ++k) {
+                        if (mbar_try_wait(&sm.empty[slot], par)) break;
+                        if ((k & 63u) == 0u) {
+                            if (*stop != 0 || *err != 0) {
+                                fail = 1;
+                                break;
+                            }
+                            if (globaltimer_ns() > deadline) {
+                                atomicCAS(const_cast<int*>(err), 0, (int)kDevTimeoutEmpty);
+                                fail = 1;
+                                break;
+                            }
+                        }
+                    }
+                }
+                if (!fail) {
+                    mbar_arrive_expect_tx(&sm.full[slot], tb);
+                    bulk_g2s(sm.ring + (size_t)slot * tb, p.wbase + ((size_t)e << 8), tb, &sm.full[slot], policy);
+                }
+            }
+            if (__shfl_sync(0xffffffffu, fail, 0)) {
+                ok = false;
+                break;
+            }
+            ++it;
+            if (++slot == nst) {
+                slot = 0;
+                par ^= 1u;
+            }
+        }
+    }
+    // Every issued copy must land before the CTA may exit.
+    if (lane == 0) {
+        const uint32_t first = it > nst ? it - nst : 0u;
+        for (uint32_t k = first; k < it; ++k) {
+            const uint64_t deadline = globaltimer_ns() + 200000000ull;
+            while (!mbar_try_wait(&sm.full[k % nst], (k / nst) & 1u)) {
+                if (globaltimer_ns() > deadline) {
+                    atomicCAS(const_cast<int*>(err), 0, (int)kDevTimeoutDrain);
+                    break;
+                }
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------- consumer helpers --
+
+__device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr)
+                 : "memory");
+}
+
+// D += A * B, m16n8k16, f16 inputs, fp32 accumulation.
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// x0, x1 (already scaled) -> packed f16 hi pair and lo pair; hi + lo = x to
+// 2^-22 relative (the subtraction is exact: hi is x rounded to 11 bits).
+__device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    hi = h2_bits(h);
+    lo = h2_bits(__floats2half2_rn(x0 - hf.x, x1 - hf.y));
+}
+
+// The staged GEMV input in act, split once per CTA: element pair p is the
+// uint2 {hi(2p, 2p+1), lo(2p, 2p+1)} of f16 pairs with x * 2^e = hi + lo to
+// 2^-22 relative (the subtraction is exact: hi is x rounded to 11 bits).
+// One scale per vector (max |x| * 2^e in [2^14, 2^15)) keeps both parts in
+// range; 2^-e goes to sh->unscale.  The thread's values v[k] are the float4
+// at index idx[k] of the vector (idx < 0: none).  Ends with a barrier.
+// `ok` is the thread's status so far; returns the CTA-uniform AND of it.
+template <int NV>
+__device__ __forceinline__ bool stage_split(const Smem& sm, const float4 (&v)[NV], const int (&idx)[NV], bool ok) {
+    const int tid = threadIdx.x, warp = tid >> 5;
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+        if (idx[k] >= 0) m = fmaxf(m, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
+    m = warp_max(m);
+    if ((tid & 31) == 0) sm.sh->rmax[warp] = m;
+    ok = !bar_red_or(kBarC, kCT, !ok);
+#pragma unroll
+    for (int k = 0; k < kCW; ++k) m = fmaxf(m, sm.sh->rmax[k]);
+    int e = 0;
+    if (m > 0.0f) {
+        e = 14 - (((__float_as_int(m) >> 23) & 0xff) - 127);
+        e = e < -126 ? -126 : (e > 126 ? 126 : e);
+    }
+    const float sc = __int_as_float((127 + e) << 23);
+    if (tid == 0) sm.sh->unscale = __int_as_float((127 - e) << 23);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        if (idx[k] >= 0) {
+            uint4 o;
+            split_pair(v[k].x * sc, v[k].y * sc, o.x, o.y);
+            split_pair(v[k].z * sc, v[k].w * sc, o.z, o.w);
+            reinterpret_cast<uint4*>(sm.act)[idx[k]] = o;
+        }
+    }
+    named_bar_sync(kBarC, kCT);
+    return ok;
+}
+
+// A fragments of the warp's column slice (KS k-steps of 16 columns) of column
+// block cb of the split input: rows 0-7 of A carry hi, rows 8-15 lo, so
+// D[g][n] + D[g+8][n] is the dot product of weight row n with x * 2^e.
+template <int KS>
+__device__ __forceinline__ void build_frags(const Smem& sm, int col0, uint32_t (&af)[KS][4]) {
+    const int warp = threadIdx.x >> 5, t = threadIdx.x & 3;
+    const uint2* base = reinterpret_cast<const uint2*>(sm.act) + (col0 + warp * (KS * 16)) / 2 + t;
+#pragma unroll
+    for (int j = 0; j < KS; ++j) {
+        const uint2 a = base[8 * j], b = base[8 * j + 4];
+        af[j][0] = a.x;
+        af[j][1] = a.y;
+        af[j][2] = b.x;
+        af[j][3] = b.y;
+    }
+}
+
+// One tile: rows 2t, 2t+1 of the tile (valid in lanes t = 0..3) over the
+// warp's column slice.
+template <int KS>
+__device__ __forceinline__ void mma_tile(uint32_t tile, const uint32_t (&af)[KS][4], float& y0, float& y1) {
+    constexpr int NS = KS < 4 ? KS : 4;  // independent accumulators
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t a = tile + warp * (KS * 256) + lane * 16;
+    uint32_t b[KS / 2][4];
+#pragma unroll
+    for (int i = 0; i < KS / 2; ++i) ldsm4(a + i * 512, b[i][0], b[i][1], b[i][2], b[i][3]);
+    float d[NS][4];
+#pragma unroll
+    for (int s = 0; s < NS; ++s) d[s][0] = d[s][1] = d[s][2] = d[s][3] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < KS / 2; ++i) {
+        mma16816(d[(2 * i) % NS], af[2 * i], b[i][0], b[i][1]);
+        mma16816(d[(2 * i + 1) % NS], af[2 * i + 1], b[i][2], b[i][3]);
+    }
+    y0 = d[0][0] + d[0][2];
+    y1 = d[0][1] + d[0][3];
+#pragma unroll
+    for (int s = 1; s < NS; ++s) {
+        y0 += d[s][0] + d[s][2];
+        y1 += d[s][1] + d[s][3];
+    }
+}
+
+// Tag of exchange k (0..5L) of step s: QKV, ATT, O, GU, DN of layer l are
+// 5l+0..5l+4, the lm_head candidates 5L.
+__device__ __forceinline__ uint32_t xtag(const DecodeParams& p, int s, int k) {
+    return p.tag_base + (uint32_t)(s * (5 * p.n_layers + 1) + k) + 1u;
+}
+
+// After an exchange's stores (all consumer threads have issued theirs),
+// thread 0 raises the CTA's flag.  The flag is a hint for when to look: the
+// data words carry their own tags, so no fence is needed -- except at the
+// end of a position (`fenced`), which orders the plain stores of the step
+// (KV-cache rows, logits) before every CTA's next position.
+__device__ __forceinline__ void publish(const DecodeParams& p, uint32_t tag, bool fenced = false) {
+    named_bar_sync(kBarC, kCT);
+    if (threadIdx.x == 0) {
+        if (fenced) fence_acq_rel_gpu();
+        st_flag(p.flags + blockIdx.x, tag);
+    }
+}
+
+// The thread's float4 chunks idx[k] (< 0: none) of a tagged vector: all
+// loads in flight together, stale chunks re-read.  Per-thread result.
+template <int NV>
+__device__ __forceinline__ bool gather_tagged(const DecodeParams& p, const uint64_t* src, const int (&idx)[NV],
+                                              uint32_t want, float4 (&v)[NV]) {
+    // All loads first (one round trip), then the tag checks.
+    uint64_t w[NV][4];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        if (idx[k] >= 0) {
+            ld_word2(src + 4 * (size_t)idx[k], w[k][0], w[k][1]);
+            ld_word2(src + 4 * (size_t)idx[k] + 2, w[k][2], w[k][3]);
+        }
+    }
+    bool fresh[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        fresh[k] = true;
+        if (idx[k] >= 0) {
+            v[k] = make_float4(__uint_as_float((uint32_t)w[k][0]), __uint_as_float((uint32_t)w[k][1]),
+                               __uint_as_float((uint32_t)w[k][2]), __uint_as_float((uint32_t)w[k][3]));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) fresh[k] = fresh[k] && (uint32_t)(w[k][j] >> 32) == want;
+        }
+    }
+    // Slow path (chunks not yet written): re-read, bounded.
+    bool ok = true;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        if (!fresh[k]) {
+            const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
+            for (uint32_t it = 1;; ++it) {
+                __nanosleep(64);
+                if (ld_tag4(src + 4 * (size_t)idx[k], want, v[k])) break;
+                if ((it & 15u) == 0u &&
+                    (*reinterpret_cast<volatile int*>(p.err) != 0 || globaltimer_ns() > deadline)) {
+                    atomicCAS(p.err, 0, (int)kDevTimeoutGrid);
+                    ok = false;
+                    break;
+                }
+            }
+        }
+    }
+    return ok;
+}
+
+// A set of CTAs whose exchange flags a reader waits for: with units > 0,
+// CTA i * G / units for i < units (all CTAs when units == G); otherwise the
+// CTAs of ranks [ra[k], rb[k]) under rotation `shift` (rank = (cta + shift)
+// % G), k < 3.
+struct FlagSet {
+    int units;
+    int shift;
+    int ra[3], rb[3];
+};
+
+__device__ __forceinline__ FlagSet all_ctas() {
+    FlagSet f;
+    f.units = gridDim.x;
+    f.shift = 0;
+    for (int k = 0; k < 3; ++k) f.ra[k] = f.rb[k] = 0;
+    return f;
+}
+
+// Rank (job_range with unit 1) that owns group g of a job with P groups.
+__device__ __forceinline__ int owner_rank(int P, int G, int g) {
+    const int base = P / G, ext = P % G;
+    if (g < ext * (base + 1)) return g / (base + 1);
+    return ext + (g - ext * (base + 1)) / base;
+}
+
+// The CTAs that run the attention units of a position with nsplit splits per
+// kv head (unit u runs on CTA u * G / units).
+__device__ __forceinline__ FlagSet attn_ctas(const DecodeParams& p, int nsplit) {
+    FlagSet f = all_ctas();
+    f.units = p.n_kv * nsplit;
+    return f;
+}
+
+// Warp 0 polls the flags of the set until all reached `want` (bounded); the
+// barrier (and with `acquire` a fence) orders the CTA's later loads after the
+// flags.  Each lane polls at most kPollPerLane flags, all loads of a round in
+// flight together.  Returns false (CTA-uniform) on timeout or a reported
+// error.
+constexpr int kPollPerLane = 8;  // grids up to 256 CTAs
+__device__ __forceinline__ bool wait_flags(const DecodeParams& p, uint32_t want, FlagSet f, bool acquire = false) {
+    bool ok = true;
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x, G = gridDim.x;
+        int n = f.units;
+        if (n == 0)
+            for (int k = 0; k < 3; ++k) n += f.rb[k] - f.ra[k];
+        const uint32_t* fp[kPollPerLane];
+#pragma unroll
+        for (int k = 0; k < kPollPerLane; ++k) {
+            const int i = lane + 32 * k;
+            int c = 0;
+            if (i < n) {
+                if (f.units > 0) {
+                    c = i * G / f.units;
+                } else {
+                    int j = i, q = 0;
+                    while (q < 2 && j >= f.rb[q] - f.ra[q]) j -= f.rb[q] - f.ra[q++];
+                    c = (f.ra[q] + j - f.shift + G) % G;
+                }
+            }
+            fp[k] = p.flags + c;
+        }
+        const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
+        for (uint32_t it = 0;; ++it) {
+            uint32_t v[kPollPerLane];
+#pragma unroll
+            for (int k = 0; k < kPollPerLane; ++k) v[k] = lane + 32 * k < n ? ld_flag(fp[k]) : want;
+            bool mine = true;
+#pragma unroll
+            for (int k = 0; k < kPollPerLane; ++k) mine &= (v[k] - want) < 0x80000000u;
+            if (__all_sync(0xffffffffu, mine)) break;
+            if ((it & 15u) == 15u) {
+                if (*reinterpret_cast<volatile int*>(p.err) != 0) {
+                    ok = false;
+                    break;
+                }
+                if (globaltimer_ns() > deadline) {
+                    if (lane == 0) atomicCAS(p.err, 0, (int)kDevTimeoutGrid);
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        if (acquire) fence_acq_rel_gpu();
+    }
+    return !bar_red_or(kBarC, kCT, !ok);
+}
+
+// Phase-trace writer (consumer thread 0): one stamp per mark().
+#if LC_DECODE_TRACE
+struct Tracer {
+    unsigned long long* base = nullptr;
+    int n = 0, cap = 0;
+    __device__ __forceinline__ void mark() { put(globaltimer_ns()); }
+    __device__ __forceinline__ void put(unsigned long long v) {
+        if (base) {
+            if (n < cap) base[n] = v;
+            ++n;
+        }
+    }
+};
+#else
+// Untraced build: every trace call compiles away.
+struct Tracer {
+    static constexpr unsigned long long* base = nullptr;
+    int n = 0, cap = 0;
+    __device__ __forceinline__ void mark() {}
+    __device__ __forceinline__ void put(unsigned long long) {}
+};
+#endif
+
+// x*invRms*w (RMSNorm.java:43,48) of a vector -> act.  The weights
+// are loaded before the exchange wait so their latency overlaps it.  src is
+// an exchange buffer (fp32, after waiting for `want`) or, when null, the
+// embedding row emb (f16).
+__device__ __forceinline__ bool stage_norm(const DecodeParams& p, const Smem& sm, const uint64_t* src,
+                                           const __half* emb, const float* __restrict__ w, uint32_t want,
+                                           Tracer& tr) {
+    const int tid = threadIdx.x, warp = tid >> 5, n4 = p.dim / 4;
+    float4 wv[2], xv[2];
+    int idx[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int i = tid + k * kCT;
+        idx[k] = i < n4 ? i : -1;
+        if (i < n4) wv[k] = __ldg(reinterpret_cast<const float4*>(w) + i);
+    }
+    bool ok = true;
+    if (src) {
+        ok = wait_flags(p, want, all_ctas());
+        tr.mark();
+        ok = gather_tagged<2>(p, src, idx, want, xv) && ok;
+        tr.mark();
+    } else {
+        tr.mark();
+        tr.mark();
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            if (idx[k] >= 0) {
+                const uint2 u = __ldg(reinterpret_cast<const uint2*>(emb) + idx[k]);
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+                xv[k] = make_float4(a.x, a.y, b.x, b.y);
+            }
+        }
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int i = tid + k * kCT;
+        if (i < n4) {
+            ss = fmaf(xv[k].x, xv[k].x, ss);
+            ss = fmaf(xv[k].y, xv[k].y, ss);
+            ss = fmaf(xv[k].z, xv[k].z, ss);
+            ss = fmaf(xv[k].w, xv[k].w, ss);
+        }
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) sm.sh->red[warp] = ss;
+    named_bar_sync(kBarC, kCT);
+    float tot = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kCW; ++k) tot += sm.sh->red[k];
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)p.dim), p.eps)));
+    float4 o[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        if (idx[k] >= 0) {
+            o[k].x = __fmul_rn(__fmul_rn(xv[k].x, inv), wv[k].x);
+            o[k].y = __fmul_rn(__fmul_rn(xv[k].y, inv), wv[k].y);
+            o[k].z = __fmul_rn(__fmul_rn(xv[k].z, inv), wv[k].z);
+            o[k].w = __fmul_rn(__fmul_rn(xv[k].w, inv), wv[k].w);
+        }
+    }
+    return stage_split<2>(sm, o, idx, ok);
+}
+
+// Attention output of all heads -> act.  One split: copy; several: merge the
+// partials (flash-decoding combine), one (head, 8 dims) per thread.  A
+// partial record is [m, l, 0, 0, o[64]] in tagged words.
+__device__ __forceinline__ bool stage_att(const DecodeParams& p, const Smem& sm, int nsplit, uint32_t want,
+                                          Tracer& tr) {
+    constexpr int HD = kAttnHeadDim;
+    bool ok = wait_flags(p, want, attn_ctas(p, nsplit));
+    tr.mark();
+    const int tid = threadIdx.x, qdim = p.n_heads * HD;
+    float4 v[2];
+    int idx[2] = {-1, -1};
+    if (nsplit == 1) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int i = tid + k * kCT;
+            if (i < qdim / 4) idx[k] = i;
+        }
+        ok = gather_tagged<2>(p, p.att, idx, want, v) && ok;
+    } else if (tid < p.n_heads * (HD / 8)) {
+        const int kv_mul = p.n_heads / p.n_kv;
+        const int H = tid / (HD / 8), d0 = (tid % (HD / 8)) * 8;
+        const uint64_t* base =
+            p.part + ((size_t)(H / kv_mul) * p.attn_max_splits * kv_mul + H % kv_mul) * kDecodePartStride;
+        const size_t sstride = (size_t)kv_mul * kDecodePartStride;
+        float M = -INFINITY, L = 0.0f, O[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) O[j] = 0.0f;
+        for (int sp = 0; sp < nsplit; ++sp) {
+            // (m, l, -, -), o[d0..d0+3], o[d0+4..d0+7] of split sp
+            const int widx[3] = {0, (4 + d0) / 4, (8 + d0) / 4};
+            float4 w[3];
+            ok = gather_tagged<3>(p, base + (size_t)sp * sstride, widx, want, w) && ok;
+            const float Mn = fmaxf(M, w[0].x);
+            const float wo = (M == -INFINITY) ? 0.0f : exp_via_double(__fsub_rn(M, Mn));
+            const float wn = exp_via_double(__fsub_rn(w[0].x, Mn));
+            L = fmaf(L, wo, w[0].y * wn);
+            const float o8[8] = {w[1].x, w[1].y, w[1].z, w[1].w, w[2].x, w[2].y, w[2].z, w[2].w};
+#pragma unroll
+            for (int c = 0; c < 8; ++c) O[c] = fmaf(O[c], wo, o8[c] * wn);
+            M = Mn;
+        }
+        const float inv = __fdiv_rn(1.0f, L);
+        v[0] = make_float4(__fmul_rn(O[0], inv), __fmul_rn(O[1], inv), __fmul_rn(O[2], inv), __fmul_rn(O[3], inv));
+        v[1] = make_float4(__fmul_rn(O[4], inv), __fmul_rn(O[5], inv), __fmul_rn(O[6], inv), __fmul_rn(O[7], inv));
+        idx[0] = (H * HD + d0) / 4;
+        idx[1] = idx[0] + 1;
+    }
+    tr.mark();
+    return stage_split<2>(sm, v, idx, ok);
+}
+
+// Sum over column blocks and warps of row r (0..7) of group gg of a batch of
+// ng groups, fixed order.
+__device__ __forceinline__ float row_sum(const float* ys, int ng, int ncb, int gg, int r) {
+    float y = 0.0f;
+    for (int cb = 0; cb < ncb; ++cb) {
+        const float4* v = reinterpret_cast<const float4*>(ys + ((cb * ng + gg) * 8 + r) * kCW);
+        const float4 a = v[0], b = v[1];
+        y += ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w));
+    }
+    return y;
+}
+
+// RoPE of one interleaved pair (RoPE.java:42-49) at position pos.
+__device__ __forceinline__ void rope_pair(float& v0, float& v1, int pos, float freq) {
+    double sd, cd;
+    sincos((double)__fmul_rn((float)pos, freq), &sd, &cd);
+    const float2 sc = make_float2((float)sd, (float)cd);
+    const float a = v0, b = v1;
+    v0 = __fsub_rn(__fmul_rn(a, sc.y), __fmul_rn(b, sc.x));
+    v1 = __fadd_rn(__fmul_rn(a, sc.x), __fmul_rn(b, sc.y));
+}
+
+struct LmState {
+    float bv;
+    int bi;
+    bool nan0;  // logits[0] is NaN (owner of row 0 only)
+};
+
+// Epilogue of one batch: groups [b0, b1) of job `kind`, ys complete; results
+// go out as tagged words with tag `tg`.  For O and DN, `res` is this thread's
+// residual x[b0 * 8 + tid] (tid < rows).
+__device__ __forceinline__ void epilogue(const DecodeParams& p, const Smem& sm, int kind, int l, int pos, int b0,
+                                         int b1, int ncb, float res, uint32_t tg, LmState& lm) {
+    constexpr int HD = kAttnHeadDim;  // decode_plan: head_dim == 64
+    const int tid = threadIdx.x, ng = b1 - b0, nrows = ng * 8;
+    const int qdim = p.n_heads * HD, kvd = p.n_kv * HD;
+    if (kind == kQKV) {
+        for (int pi = tid; pi < nrows / 2; pi += kCT) {
+            const int gg = pi >> 2, r = (pi & 3) * 2, R = (b0 + gg) * 8 + r;
+            float y0 = row_sum(sm.ys, ng, 1, gg, r), y1 = row_sum(sm.ys, ng, 1, gg, r + 1);
+            // q rows, then k rows, then v rows; k and q are rotated.
+            const int kv = R < qdim ? -1 : (R < qdim + kvd ? 0 : 1);
+            const int rr = R - (kv < 0 ? 0 : qdim + kv * kvd), i = rr & (HD - 1);
+            if (kv <= 0) rope_pair(y0, y1, pos, p.rope.f[i >> 1]);
+            if (kv < 0) {
+                st_tag2(p.q + R, y0, y1, tg);
+            } else {
+                // the KV cache (plain, read at later positions) and this
+                // position's k / v for the attention units (tagged)
+                float* dst = (kv == 0 ? p.kcache : p.vcache) + (((size_t)l * p.n_kv + rr / HD) * p.max_seq + pos) * HD + i;
+                *reinterpret_cast<float2*>(dst) = make_float2(y0, y1);
+                st_tag2(p.kv + kv * kvd + rr, y0, y1, tg);
+            }
+        }
+    } else if (kind == kGU) {
+        // rows 4m..4m+3 = (gate, up) of h[2m], h[2m+1] (TransformerBlock.java:205-209)
+        for (int pi = tid; pi < nrows / 4; pi += kCT) {
+            const int gg = pi >> 1, r = (pi & 1) * 4, R = (b0 + gg) * 8 + r;
+            const float h0 = __fmul_rn(silu_ref(row_sum(sm.ys, ng, 1, gg, r)), row_sum(sm.ys, ng, 1, gg, r + 1));
+            const float h1 = __fmul_rn(silu_ref(row_sum(sm.ys, ng, 1, gg, r + 2)), row_sum(sm.ys, ng, 1, gg, r + 3));
+            *reinterpret_cast<float2*>(p.h + (R >> 1)) = make_float2(h0, h1);
+        }
+    } else if (kind == kLM) {
+        for (int k = tid; k < nrows; k += kCT) {
+            const int R = b0 * 8 + k;
+            if (R < p.vocab) {
+                const float v = row_sum(sm.ys, ng, 1, k >> 3, k & 7);
+                p.logits[R] = v;
+                if (R == 0 && v != v) lm.nan0 = true;
+                if (v == v && (lm.bi < 0 || v > lm.bv)) {
+                    lm.bv = v;
+                    lm.bi = R;
+                }
+            }
+        }
+    } else if (tid < nrows) {  // O, DN: residual add (TransformerBlock.java:195-198, 211-216)
+        uint64_t* out = (kind == kO) ? p.xa : p.xb;
+        st_tag1(out + b0 * 8 + tid, __fadd_rn(res, row_sum(sm.ys, ng, ncb, tid >> 3, tid & 7)), tg);
+    }
+}
+
+LC_DEV uint64_t ld_word(const uint64_t* p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+
+// Value of tagged word w loaded from src; re-read until it carries `want`
+// (bounded).  For residuals, which the prologue already saw complete.
+__device__ __forceinline__ bool resolve_tagged1(const DecodeParams& p, const uint64_t* src, uint64_t w, uint32_t want,
+                                                float* v) {
+    const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
+    for (uint32_t it = 0; (uint32_t)(w >> 32) != want; ++it) {
+        if ((it & 15u) == 15u && (*reinterpret_cast<volatile int*>(p.err) != 0 || globaltimer_ns() > deadline)) {
+            atomicCAS(p.err, 0, (int)kDevTimeoutGrid);
+            return false;
+        }
+        __nanosleep(64);
+        w = ld_word(src);
+    }
+    *v = __uint_as_float((uint32_t)w);
+    return true;
+}
+
+// Shared-memory view from the dynamic shared-memory base and the
+// compile-time layout (no registers needed for it).
+template <int KS>
+__device__ __forceinline__ Smem smem_view() {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    constexpr Layout L = LayoutOf<KS>::L;
+    Smem sm;
+    sm.ring = smem_raw;
+    sm.full = reinterpret_cast<uint64_t*>(smem_raw + L.off_bar);
+    sm.empty = sm.full + kMaxStages;
+    sm.sh = reinterpret_cast<Shared*>(smem_raw + L.off_sh);
+    sm.act = reinterpret_cast<float*>(smem_raw + L.off_act);
+    sm.ys = reinterpret_cast<float*>(smem_raw + L.off_ys);
+    sm.stages = L.stages;
+    sm.tile_bytes = L.tile_bytes;
+    return sm;
+}
+
+struct RingPos {
+    uint32_t slot, par;         // next stage and its phase parity
+    int ok;                     // every stage so far was seen landing
+    unsigned long long waited;  // trace only: thread 0's ns waiting for stages
+};
+
+// The tiles of one batch (column blocks 0..ncb-1, groups [b0, b1)) into ys.
+// Out of line: the hot loop gets a register allocation of its own, with
+// nothing of the caller's state live in it.
+template <int KS>
+__device__ __noinline__ RingPos consume_batch(const DecodeParams& p, RingPos r, int b0, int b1, int ncb, bool timing) {
+    const Smem sm = smem_view<KS>();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, ng = b1 - b0;
+    const uint32_t ring = smem_u32(sm.ring);
+    const float unscale = sm.sh->unscale;
+    for (int cb = 0; cb < ncb; ++cb) {
+        uint32_t af[KS][4];
+        build_frags<KS>(sm, cb * p.dim, af);
+#pragma unroll 1
+        for (int g = b0; g < b1; ++g) {
+            const unsigned long long t0 = timing ? globaltimer_ns() : 0ull;
+            bool got = r.ok && (mbar_try_wait(&sm.full[r.slot], r.par) ||
+                                mbar_wait_bounded(&sm.full[r.slot], r.par, p.err, globaltimer_ns() + p.timeout_ns,
+                                                  kDevTimeoutFull));
+            // ldmatrix / mma are warp-collective: the whole warp takes the same
+            // branch.  A stage that was not seen landing is never released
+            // (the producer then stops on the error word).
+            got = __all_sync(0xffffffffu, got);
+            if (timing) r.waited += globaltimer_ns() - t0;
+            float y0 = 0.0f, y1 = 0.0f;
+            if (got) {
+                mma_tile<KS>(ring + r.slot * (uint32_t)sm.tile_bytes, af, y0, y1);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.empty[r.slot]);
+            } else {
+                r.ok = 0;
+            }
+            if (lane < 4) {
+                float* yo = sm.ys + ((cb * ng + (g - b0)) * 8 + 2 * lane) * kCW + warp;
+                yo[0] = y0 * unscale;
+                yo[kCW] = y1 * unscale;
+            }
+            if (++r.slot == (uint32_t)sm.stages) {
+                r.slot = 0;
+                r.par ^= 1u;
+            }
+        }
+    }
+    return r;
+}
+
+// The CTA's groups [g0, g1) of one job: batches of tiles through the ring,
+// epilogue per batch.  The only place tiles are consumed.
+template <int KS>
+__device__ __forceinline__ bool consume_job(const DecodeParams& p, const Smem& sm, RingPos& ring, int kind, int l,
+                                            int pos, int g0, int g1, int ncb, const uint64_t* res_src,
+                                            uint32_t res_tag, const __half* res_emb, uint32_t out_tag, LmState& lm,
+                                            Tracer& tr) {
+    const int tid = threadIdx.x;
+    const int bg = batch_groups(ncb);
+    bool ok = true;
+    for (int b0 = g0; b0 < g1; b0 += bg) {
+        const int b1 = min(g1, b0 + bg), ng = b1 - b0;
+        // Residual of the thread's row (O, DN): requested now, used in the epilogue.
+        const bool has_res = (kind == kO || kind == kDN) && tid < ng * 8;
+        uint64_t resw = 0;
+        float res = 0.0f;
+        if (has_res) {
+            if (res_src) resw = ld_word(res_src + b0 * 8 + tid);
+            else res = __half2float(res_emb[b0 * 8 + tid]);
+        }
+        if (b0 == g0) tr.mark();
+        ring.waited = 0;
+        ring = consume_batch<KS>(p, ring, b0, b1, ncb, tr.base != nullptr);
+        named_bar_sync(kBarC, kCT);
+        if (b0 == g0) {
+            tr.mark();
+            tr.put(ring.waited);
+        }
+        if (has_res && res_src) ok = resolve_tagged1(p, res_src + b0 * 8 + tid, resw, res_tag, &res) && ok;
+        epilogue(p, sm, kind, l, pos, b0, b1, ncb, res, out_tag, lm);
+        named_bar_sync(kBarC, kCT);
+        if (b0 == g0) tr.mark();
+    }
+    if (g0 >= g1) {
+        tr.mark();
+        tr.mark();
+        tr.put(0);
+        tr.mark();
+    }
+    return ok && ring.ok;
+}
+
+// ------------------------------------------------------------- consumer --
+
+// One attention unit: positions [t0, t1) of kv head kvh for its kv_mul query
+// heads at position pos.  Same arithmetic as attention_core
+// (lc_attention.cuh), so a single split is bit-identical to the Java kernels:
+// sequential score dot products (Attention.java:36-40), max, exp in double,
+// sequential sum, p = e * (1/sum) (Softmax.java:30-50), sequential weighted
+// values (Attention.java:54-60).  K rows of earlier positions (plain fp32
+// cache, written at earlier positions) are requested before the wait for
+// this position's q, k and v (tagged words), which waits only for the CTAs
+// that own those rows of the QKV job (rotation `qkv_shift`).  K, then V,
+// pass through shared memory kVChunk positions at a time.
+__device__ __forceinline__ bool attn_unit(const DecodeParams& p, int s, int l, int pos, int kvh, int t0, int t1,
+                                          int nsplit, int sp, int qkv_shift, float* sm, Tracer& tr) {
+    constexpr int HD = kAttnHeadDim, VPT = kVChunk * HD / 4 / kCT;  // float4 of a chunk per thread
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, G = gridDim.x;
+    const int kv_mul = p.n_heads / p.n_kv, T = t1 - t0, pr = pos - t0;  // pr: row of pos in the unit
+    const int qdim = p.n_heads * HD, kvd = p.n_kv * HD;
+    const uint32_t in_tag = xtag(p, s, 5 * l + 0), out_tag = xtag(p, s, 5 * l + 1);
+    float* qs = sm;
+    float* cur = qs + kv_mul * HD;  // this position's k, v
+    float* kvs = cur + 2 * HD;
+    float* sc = kvs + kVChunk * HD;
+    float* st = sc + kv_mul * kAttnTmax;
+    const size_t kvbase = (((size_t)l * p.n_kv + kvh) * p.max_seq + t0) * HD;
+    const float4* K4 = reinterpret_cast<const float4*>(p.kcache + kvbase);
+    const float4* V4 = reinterpret_cast<const float4*>(p.vcache + kvbase);
+    // Rows [c0, c0 + n) of K or V (cache, without row pos) -> kvs, by threads
+    // t0th.. of the CTA: all loads in flight, then the stores.
+    auto load_rows = [&](const float4* src, int c0, int t0th) {
+        constexpr int R = (kVChunk * HD / 4 + kCT - 32 - 1) / (kCT - 32);  // float4 per thread, at most
+        const int n4 = min(kVChunk, T - c0) * (HD / 4), step = kCT - t0th, i0 = tid - t0th;
+        float4 r[R];
+#pragma unroll
+        for (int k = 0; k < R; ++k) {
+            const int i = i0 + k * step;
+            if (i0 >= 0 && i < n4 && c0 + i / (HD / 4) != pr) r[k] = __ldcg(src + (size_t)c0 * (HD / 4) + i);
+        }
+#pragma unroll
+        for (int k = 0; k < R; ++k) {
+            const int i = i0 + k * step;
+            if (i0 >= 0 && i < n4 && c0 + i / (HD / 4) != pr) reinterpret_cast<float4*>(kvs)[i] = r[k];
+        }
+    };
+    // Row pos of the chunk at c0 from cur (k: which = 0, v: 1).
+    auto put_cur = [&](int c0, int which) {
+        if (pr >= c0 && pr < c0 + kVChunk && tid < HD / 4)
+            reinterpret_cast<float4*>(kvs)[(pr - c0) * (HD / 4) + tid] =
+                reinterpret_cast<const float4*>(cur + which * HD)[tid];
+    };
+    load_rows(K4, 0, 32);  // warp 0 starts polling at once
+    // Owners of q rows (heads of this kv head), k rows and v rows of kvh.
+    FlagSet f;
+    f.units = 0;
+    f.shift = qkv_shift;
+    {
+        const int P = (qdim + 2 * kvd) / 8;
+        const int ga[3] = {kvh * kv_mul * HD / 8, (qdim + kvh * HD) / 8, (qdim + kvd + kvh * HD) / 8};
+        const int gn[3] = {kv_mul * HD / 8, HD / 8, HD / 8};
+        for (int k = 0; k < 3; ++k) {
+            f.ra[k] = owner_rank(P, G, ga[k]);
+            f.rb[k] = owner_rank(P, G, ga[k] + gn[k] - 1) + 1;
+        }
+    }
+    bool ok = wait_flags(p, in_tag, f);
+    tr.mark();
+    // q and this position's k, v (tagged), one float4 per thread; the first
+    // V chunk (cache rows) in registers meanwhile.
+    {
+        const int nq = kv_mul * HD / 4;
+        const uint64_t* src = nullptr;
+        float* dst = nullptr;
+        if (tid < nq) {
+            src = p.q + ((size_t)kvh * kv_mul * HD + 4 * tid);
+            dst = qs + 4 * tid;
+        } else if (tid < nq + HD / 2) {
+            const int j = tid - nq, which = j / (HD / 4), e = (j % (HD / 4)) * 4;
+            src = p.kv + (size_t)which * kvd + kvh * HD + e;
+            dst = cur + which * HD + e;
+        }
+        if (src) {
+            const int one[1] = {0};
+            float4 v[1];
+            ok = gather_tagged<1>(p, src, one, in_tag, v) && ok;
+            *reinterpret_cast<float4*>(dst) = v[0];
+        }
+    }
+    float4 vr[VPT];
+    {
+        const int n4 = min(kVChunk, T) * (HD / 4);
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            const int i = tid + k * kCT;
+            if (i < n4 && i / (HD / 4) != pr) vr[k] = __ldcg(V4 + i);
+        }
+    }
+    ok = !bar_red_or(kBarC, kCT, !ok);
+    // Scores, chunk by chunk: consecutive threads take the kv_mul heads of one position.
+    for (int c0 = 0; c0 < T; c0 += kVChunk) {
+        if (c0 > 0) {
+            named_bar_sync(kBarC, kCT);  // previous chunk's scores done
+            load_rows(K4, c0, 0);
+        }
+        put_cur(c0, 0);
+        named_bar_sync(kBarC, kCT);
+        const int n = min(kVChunk, T - c0);
+        for (int idx = tid; idx < n * kv_mul; idx += kCT) {
+            const int h = idx % kv_mul, tt = idx / kv_mul;
+            const float* kr = kvs + tt * HD;
+            const float* qh = qs + h * HD;
+            float sum = 0.0f;
+#pragma unroll 16
+            for (int i = 0; i < HD; ++i) sum = __fadd_rn(sum, __fmul_rn(qh[i], kr[i]));
+            sc[h * kAttnTmax + c0 + tt] = __fmul_rn(sum, p.attn_scale);
+        }
+    }
+    tr.mark();
+    named_bar_sync(kBarC, kCT);
+    // Per head: max, e = exp(s - max), sum.  The first V chunk replaces K.
+    {
+        const int n4 = min(kVChunk, T) * (HD / 4);
+#pragma unroll
+        for (int k = 0; k < VPT; ++k) {
+            const int i = tid + k * kCT;
+            if (i < n4 && i / (HD / 4) != pr) reinterpret_cast<float4*>(kvs)[i] = vr[k];
+        }
+        put_cur(0, 1);
+    }
+    for (int h = warp; h < kv_mul; h += kCW) {
+        float* e = sc + h * kAttnTmax;
+        float m = -INFINITY;
+        for (int t = lane; t < T; t += 32) m = fmaxf(m, e[t]);
+        m = warp_max(m);
+        for (int t = lane; t < T; t += 32) e[t] = exp_via_double(__fsub_rn(e[t], m));
+        __syncwarp();
+        float lsum = 0.0f;
+        if (nsplit == 1) {
+            if (lane == 0)
+                for (int t = 0; t < T; ++t) lsum = __fadd_rn(lsum, e[t]);
+            lsum = __shfl_sync(0xffffffffu, lsum, 0);
+        } else {
+            for (int t = lane; t < T; t += 32) lsum += e[t];
+            lsum = warp_sum(lsum);
+        }
+        if (lane == 0) {
+            st[2 * h] = m;
+            st[2 * h + 1] = lsum;
+        }
+    }
+    named_bar_sync(kBarC, kCT);
+    tr.mark();
+    // Weighted values: thread per (head, dim), sequential over positions.
+    float acc[2] = {0.0f, 0.0f};  // kv_mul * HD <= 2 * kCT
+    for (int c0 = 0; c0 < T; c0 += kVChunk) {
+        if (c0 > 0) {
+            named_bar_sync(kBarC, kCT);  // previous chunk fully read
+            load_rows(V4, c0, 0);
+            put_cur(c0, 1);
+            named_bar_sync(kBarC, kCT);
+        }
+        const int n = min(kVChunk, T - c0);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int hi = tid + k * kCT;
+            if (hi < kv_mul * HD) {
+                const int h = hi / HD, i = hi % HD;
+                const float* e = sc + h * kAttnTmax + c0;
+                float a = acc[k];
+                if (nsplit == 1) {
+                    const float inv = __fdiv_rn(1.0f, st[2 * h + 1]);
+                    for (int t = 0; t < n; ++t) a = __fadd_rn(a, __fmul_rn(__fmul_rn(e[t], inv), kvs[t * HD + i]));
+                } else {
+                    for (int t = 0; t < n; ++t) a = fmaf(e[t], kvs[t * HD + i], a);
+                }
+                acc[k] = a;
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int hi = tid + k * kCT;
+        if (hi < kv_mul * HD) {
+            const int h = hi / HD, i = hi % HD;
+            if (nsplit == 1) {
+                st_tag1(p.att + ((size_t)kvh * kv_mul + h) * HD + i, acc[k], out_tag);
+            } else {
+                uint64_t* pp = p.part + (((size_t)kvh * p.attn_max_splits + sp) * kv_mul + h) * kDecodePartStride;
+                st_tag1(pp + 4 + i, acc[k], out_tag);
+                if (i == 0) {
+                    st_tag2(pp, st[2 * h], st[2 * h + 1], out_tag);
+                    st_tag2(pp + 2, 0.0f, 0.0f, out_tag);
+                }
+            }
+        }
+    }
+    return ok;
+}
+
+// Attention units of layer l at position pos: unit u = (kv head, split) runs
+// on CTA u * G / units.
+__device__ __forceinline__ bool run_attention(const DecodeParams& p, const Smem& sm, int s, int l, int pos,
+                                              int qkv_shift, Tracer& tr) {
+    const int G = gridDim.x, cta = blockIdx.x, seq = pos + 1;
+    const int T = attn_split_len(seq, G, p.n_kv), nsplit = (seq + T - 1) / T, units = p.n_kv * nsplit;
+    bool ok = true;
+    const int trace_n = tr.n;
+    // units * G < 2^31 (units <= n_kv * max splits)
+    for (int u = (cta * units + G - 1) / G; u < units && (u * G) / units == cta; ++u) {
+        const int kvh = u / nsplit, sp = u % nsplit;
+        const int t0 = sp * T, t1 = min(seq, t0 + T);
+        ok &= attn_unit(p, s, l, pos, kvh, t0, t1, nsplit, sp, qkv_shift, sm.act, tr);
+        named_bar_sync(kBarC, kCT);
+        tr.mark();
+    }
+    // Fixed trace layout: four stamps per layer (first unit), with or without
+    // units.  (Only thread 0 records; the loop is bounded for every thread.)
+    for (int k = tr.n - trace_n; k < 4; ++k) tr.mark();
+    if (tr.base) tr.n = trace_n + 4;
+    return ok;
+}
+
+// h (all hidden floats) -> act, after the gate/up exchange.
+__device__ __forceinline__ bool stage_h(const DecodeParams& p, const Smem& sm, uint32_t want, Tracer& tr) {
+    // h is plain fp32 (half the bytes of tagged words): the gate/up
+    // epilogues publish it with a fence, the flags are read with acquire.
+    constexpr int NV = 8;  // float4 per thread: hidden <= 8 * 4 * kCT (decode_plan)
+    const bool ok = wait_flags(p, want, all_ctas(), true);
+    tr.mark();
+    float4 v[NV];
+    int idx[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        const int i = threadIdx.x + k * kCT;
+        idx[k] = i < p.hidden / 4 ? i : -1;
+        if (idx[k] >= 0) v[k] = __ldcg(reinterpret_cast<const float4*>(p.h) + i);
+    }
+    tr.mark();
+    return stage_split<NV>(sm, v, idx, ok);
+}
+
+// lm_head epilogue: the CTA's argmax candidate (LlamaInference.argmax
+// semantics, :252-262) goes out, then every CTA merges all candidates.
+__device__ __forceinline__ bool argmax_exchange(const DecodeParams& p, const Smem& sm, int s, const LmState& lm,
+                                                int* next) {
+    const int G = gridDim.x, cta = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t tag = xtag(p, s, 5 * p.n_layers);
+    float bv = lm.bv;
+    int bi = lm.bi;
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        argmax_merge(bv, bi, v2, i2);
+    }
+    const bool nan0 = bar_red_or(kBarC, kCT, lm.nan0);
+    if (lane == 0) {
+        sm.sh->bv[warp] = bv;
+        sm.sh->bi[warp] = bi;
+    }
+    named_bar_sync(kBarC, kCT);
+    if (tid == 0) {
+        float B = sm.sh->bv[0];
+        int I = sm.sh->bi[0];
+        for (int w = 1; w < kCW; ++w) argmax_merge(B, I, sm.sh->bv[w], sm.sh->bi[w]);
+        // NaN in logits[0] makes the Java argmax return 0 (nothing is '>'
+        // NaN): the owner of row 0 offers (+inf, 0), which wins.
+        if (nan0) {
+            B = INFINITY;
+            I = 0;
+        }
+        st_tag2(p.amax + 2 * cta, B, __int_as_float(I), tag);
+    }
+    // The end of a position: fenced, so the step's plain stores (KV-cache
+    // rows, h) are visible to every CTA's next position.
+    publish(p, tag, true);
+    bool ok = wait_flags(p, tag, all_ctas(), true);
+    if (warp == 0) {
+        float B = -INFINITY;
+        int I = -1;
+        float2 v[kPollPerLane];
+        bool got[kPollPerLane];
+#pragma unroll
+        for (int k = 0; k < kPollPerLane; ++k)
+            got[k] = lane + 32 * k < G && ld_tag2(p.amax + 2 * (lane + 32 * k), tag, v[k]);
+#pragma unroll
+        for (int k = 0; k < kPollPerLane; ++k) {
+            if (lane + 32 * k < G) {
+                // cannot fail after the fenced exchange
+                if (!got[k]) ok = false;
+                else argmax_merge(B, I, v[k].x, __float_as_int(v[k].y));
+            }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float v2 = __shfl_xor_sync(0xffffffffu, B, o);
+            const int i2 = __shfl_xor_sync(0xffffffffu, I, o);
+            argmax_merge(B, I, v2, i2);
+        }
+        if (lane == 0) sm.sh->next = I < 0 ? 0 : I;
+    }
+    ok = !bar_red_or(kBarC, kCT, !ok);
+    *next = *reinterpret_cast<volatile int*>(&sm.sh->next);
+    return ok;
+}
+
+// One position = jobs j = 0 .. 4L-1 (layer j/4, kind j%4) and, when logits
+// are needed, the lm_head job j = 4L.  Every job is: prologue (exchange
+// wait + staging), consume_job, publish, then the attention units after QKV
+// and the argmax exchange after LM.  Each piece appears once in the code.
+template <int KS>
+__device__ __forceinline__ void run_consumer(const DecodeParams& p, const Smem& sm) {
+    const int G = gridDim.x, cta = blockIdx.x, tid = threadIdx.x, NL = p.n_layers;
+    Tracer tr;
+#if LC_DECODE_TRACE
+    if (p.trace && tid == 0) {
+        tr.base = p.trace + (size_t)cta * p.trace_words;
+        tr.cap = p.trace_words;
+    }
+#endif
+    Rotation rot;
+    int qkv_shift = 0;  // rotation of the current layer's QKV job
+    RingPos ring;
+    ring.slot = 0;
+    ring.par = 0;
+    ring.ok = 1;
+    ring.waited = 0;
+    int next = 0, steps_done = 0;
+    bool ok = true;
+    LmState lm;
+    lm.bv = -INFINITY;
+    lm.bi = -1;
+    lm.nan0 = false;
+
+    for (int s = 0; s < p.nsteps; ++s) {
+        const int pos = p.pos0 + s;
+        const int token = (s == 0 || pos < p.n_prompt) ? __ldcg(p.tokens + pos) : next;
+        if (token < 0 || token >= p.vocab) {
+            if (cta == 0 && tid == 0) atomicCAS(p.err, 0, (int)kDevBadToken);
+            ok = false;
+        }
+        // Leave on a CTA-uniform decision only.
+        if (bar_red_or(kBarC, kCT, !ok || *reinterpret_cast<volatile int*>(p.err) != 0)) break;
+        const __half* emb = p.tok_emb + (size_t)token * (size_t)p.dim;
+        rot = Rotation();  // every position deals rows alike (the producer's tile list)
+        const int seq = pos + 1;
+        const int nsplit = (seq + attn_split_len(seq, G, p.n_kv) - 1) / attn_split_len(seq, G, p.n_kv);
+        const int njobs = 4 * NL + (lm_needed(p, pos) ? 1 : 0);
+
+#pragma unroll 1
+        for (int j = 0; j < njobs; ++j) {
+            const int kind = (j == 4 * NL) ? (int)kLM : (j & 3), l = (j == 4 * NL) ? NL - 1 : (j >> 2);
+            const LayerW* LW = p.layers + l;
+            // Exchange this job waits for: the previous job's output.
+            const uint32_t want = xtag(p, s, 5 * l + (kind == kQKV ? -1 : kind == kO ? 1 : kind == kGU ? 2 : kind == kDN ? 3 : 4));
+            tr.mark();
+            const JobGeo jg = job_geo(p, p.layers, kind, l);
+            int g0, g1;
+            if (kind == kQKV) qkv_shift = rot.shift;
+            job_range(jg.groups, 1, G, rot.rank(cta, G), &g0, &g1);
+            rot.advance(jg.groups, 1, G);
+            if (kind == kO) {
+                ok &= stage_att(p, sm, nsplit, want, tr);
+            } else if (kind == kDN) {
+                ok &= stage_h(p, sm, want, tr);
+            } else {
+                const bool first = (kind == kQKV && l == 0);
+                const float* w = (kind == kQKV) ? LW->attn_norm : (kind == kGU) ? LW->ffn_norm : p.out_norm;
+                // x after O for GU, after DN (previous layer) for QKV and LM
+                ok &= stage_norm(p, sm, first ? nullptr : (kind == kGU ? p.xa : p.xb), emb, w, want, tr);
+            }
+            if (kind == kLM) {
+                lm.bv = -INFINITY;
+                lm.bi = -1;
+                lm.nan0 = false;
+            }
+            tr.mark();
+            // residual of O: x of the block input (embedding in layer 0); of DN: x after O
+            const uint64_t* res_src = (kind == kDN) ? p.xa : (l == 0 ? nullptr : p.xb);
+            const uint32_t res_tag = (kind == kDN) ? xtag(p, s, 5 * l + 2) : xtag(p, s, 5 * l - 1);
+            // kinds QKV, O, GU, DN publish exchanges 5l + 0, 2, 3, 4
+            const uint32_t out_tag = xtag(p, s, 5 * l + (kind == kQKV ? 0 : kind + 1));
+            ok &= consume_job<KS>(p, sm, ring, kind, l, pos, g0, g1, jg.ncb, res_src, res_tag, emb, out_tag, lm, tr);
+            if (kind == kLM) {
+                ok &= argmax_exchange(p, sm, s, lm, &next);
+            } else {
+                publish(p, out_tag, kind == kGU);  // h is plain fp32: fenced
+                if (kind == kQKV) {
+                    tr.mark();
+                    ok &= run_attention(p, sm, s, l, pos, qkv_shift, tr);
+                    publish(p, xtag(p, s, 5 * l + 1));
+                }
+            }
+            tr.mark();
+        }
+
+        if (!lm_needed(p, pos)) {
+            // End of a position without logits: the same fenced exchange.
+            publish(p, xtag(p, s, 5 * NL), true);
+            ok &= wait_flags(p, xtag(p, s, 5 * NL), all_ctas(), true);
+        }
+        bool stop_now = false;
+        if (lm_needed(p, pos) && pos + 1 >= p.n_prompt) {
+            if (cta == 0 && tid == 0) p.tokens[pos + 1] = next;
+            for (int k = 0; k < p.n_stop; ++k) stop_now |= (p.stop[k] == next);
+        }
+        if (ok) steps_done = s + 1;
+        if (stop_now) break;
+    }
+    if (tid == 0) {
+        sm.sh->stop = 1;
+        if (cta == 0) *p.n_done = steps_done;
+    }
+}
+
+template <int KS>
+__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
+    constexpr Layout L = LayoutOf<KS>::L;
+    const Smem sm = smem_view<KS>();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < L.stages; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], kCW);
+        }
+        sm.sh->stop = 0;
+        sm.sh->next = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x >= kCT) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegProducer));
+        if (threadIdx.x < kCT + 32) run_producer(p, sm);
+        return;
+    }
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegConsumer));
+    run_consumer<KS>(p, sm);
+}
+
+template <int KS>
+cudaError_t launch_ks(const DecodeParams& p, const DecodeLaunch& l, cudaStream_t st) {
+    void* args[] = {const_cast<DecodeParams*>(&p)};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(l.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = l.smem_bytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, (const void*)decode_kernel<KS>, args);
+}
+
+// Sets the shared-memory attribute and checks the register count the
+// setmaxnreg split is built on: with fewer registers per thread at launch the
+// pool could not serve the consumers' increase.
+template <int KS>
+cudaError_t set_smem(int bytes) {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, decode_kernel<KS>);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != kRegLaunch) return cudaErrorInvalidKernelImage;
+    return cudaFuncSetAttribute(decode_kernel<KS>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+cudaError_t impl_prepare(const DecodeLaunch& l) {
+    switch (l.ks) {
+        case 2: return set_smem<2>(l.smem_bytes);
+        case 4: return set_smem<4>(l.smem_bytes);
+        case 8: return set_smem<8>(l.smem_bytes);
+        default: return set_smem<16>(l.smem_bytes);
+    }
+}
+
+cudaError_t impl_launch(const DecodeParams& p, const DecodeLaunch& l, cudaStream_t st) {
+    switch (l.ks) {
+        case 2: return launch_ks<2>(p, l, st);
+        case 4: return launch_ks<4>(p, l, st);
+        case 8: return launch_ks<8>(p, l, st);
+        default: return launch_ks<16>(p, l, st);
+    }
+}
+
+}  // namespace
+}  // namespace lc

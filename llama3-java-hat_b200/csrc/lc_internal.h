@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <vector>
+
 #include "lc_common.cuh"
 
 namespace lc {
@@ -84,7 +86,7 @@ cudaError_t launch_tile_rows(const __half* src, __half* dst, int rows, int cols,
                              cudaStream_t st);
 
 constexpr int kMaxStop = 32;
-constexpr int kDecodePartStride = 68;  // floats per attention partial: m, l, o[64], pad
+constexpr int kDecodePartStride = 68;  // words per attention partial: m, l, 0, 0, o[64]
 
 struct DecodeParams {
     // model
@@ -103,15 +105,17 @@ struct DecodeParams {
     int32_t* tokens;       // [max_seq + 1]: token fed at each position
     int* err;              // device error word
     int* n_done;           // steps completed
-    // Exchange buffers, published through per-CTA flags.
-    float* xa;             // [dim]   x after the attention residual
-    float* xb;             // [dim]   x after the FFN residual
-    float* q;              // [n_heads*head_dim] rotated q of the current position
-    float* att;            // [n_heads*head_dim] attention output (single split)
-    float* part;           // [n_kv][attn_max_splits][kv_mul][kDecodePartStride] partials
-    float* h;              // [hidden] silu(gate)*up
-    float* amax;           // [grid][2] per-CTA argmax candidate (value, index bits)
-    uint32_t* flags;       // [grid] latest exchange tag each CTA has published
+    // Exchange buffers: tagged 64-bit words (float bits | tag << 32); the
+    // per-CTA flags say when to look, the tags say what is valid.
+    uint64_t* xa;          // [dim]   x after the attention residual
+    uint64_t* xb;          // [dim]   x after the FFN residual
+    uint64_t* q;           // [n_heads*head_dim] rotated q of the current position
+    uint64_t* kv;          // [2*kv_dim] rotated k, then v, of the current position
+    uint64_t* att;         // [n_heads*head_dim] attention output (single split)
+    uint64_t* part;        // [n_kv][attn_max_splits][kv_mul][kDecodePartStride] partials
+    float* h;              // [hidden] silu(gate)*up (plain: published with a fence)
+    uint64_t* amax;        // [grid][2] per-CTA argmax candidate (value, index bits)
+    uint32_t* flags;       // [grid] latest exchange tag each CTA has published (a hint)
     uint32_t tag_base;     // launch epoch << 20; tags are tag_base + exchange + 1
     // launch
     int pos0, nsteps, n_prompt;
@@ -124,9 +128,14 @@ struct DecodeParams {
     // %globaltimer stamps into trace[cta*trace_words + k].
     unsigned long long* trace;
     int trace_words;
-    // Producer L2 prefetch distance, in tiles beyond the tile being copied
-    // into shared memory (0 = no L2 prefetch).
-    int l2_prefetch_stages;
+    // Producer tile schedule of one position (decode_build_schedule): row
+    // cta * sched_stride of `sched` lists the CTA's weight tiles in consumption
+    // order as offsets from wbase in 256-byte units, the QKV..DN jobs of all
+    // layers (sched_n[2 * cta] tiles) then the lm_head job (sched_n[2 * cta + 1]).
+    const uint32_t* sched;
+    const int* sched_n;
+    int sched_stride;
+    const uint8_t* wbase;
 };
 
 struct DecodeLaunch {
@@ -140,10 +149,19 @@ struct DecodeLaunch {
 // layout of DecodeParams::part).
 int decode_attn_max_splits(int max_seq, int grid, int n_kv);
 
+// Host: the producer tile schedule of one position for a grid of G CTAs
+// (DecodeParams::sched): p's model fields with host copies of the layer
+// table in `layers`.  Fills rows of `stride` entries and per-CTA counts.
+void decode_build_schedule(const DecodeParams& p, const LayerW* layers, int G, std::vector<uint32_t>* sched,
+                           std::vector<int>* counts, int* stride);
+
 // Validates the configuration against what the fused kernel implements and
 // fills the launch shape.  Returns false with a message when unsupported.
 bool decode_plan(const DecodeParams& p, int num_sms, DecodeLaunch* out, const char** why);
 cudaError_t decode_prepare(const DecodeLaunch& l);  // sets the smem attribute once
 cudaError_t launch_decode(const DecodeParams& p, const DecodeLaunch& l, cudaStream_t st);
+// Same kernel built with the phase trace (p.trace must be set).
+cudaError_t decode_prepare_traced(const DecodeLaunch& l);
+cudaError_t launch_decode_traced(const DecodeParams& p, const DecodeLaunch& l, cudaStream_t st);
 
 }  // namespace lc

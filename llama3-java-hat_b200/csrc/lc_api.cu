@@ -508,6 +508,7 @@ struct lc_model {
     bool finalized = false;
     RopeFreq rope;
     DecodeLaunch launch;
+    int l2_prefetch_tiles = 0;    // producer L2 prefetch window (tiles)
     uint32_t* d_sched = nullptr;  // producer tile schedule (decode_build_schedule)
     int* d_sched_n = nullptr;
     int sched_stride = 0;
@@ -762,6 +763,7 @@ static void fill_model_params(const lc_model* m, DecodeParams* p) {
     p->sched_n = m->d_sched_n;
     p->sched_stride = m->sched_stride;
     p->wbase = (const uint8_t*)m->arena;
+    p->l2_prefetch_tiles = m->l2_prefetch_tiles;
 }
 
 extern "C" int lc_model_finalize(lc_model* m) {
@@ -783,6 +785,7 @@ extern "C" int lc_model_finalize(lc_model* m) {
     m->staging = nullptr;
     m->staging_bytes = 0;
     make_rope_freq(&m->rope, m->cfg.rope_theta, m->cfg.head_dim);
+    if (const char* e = getenv("LLAMACUDA_L2_PREFETCH_TILES")) m->l2_prefetch_tiles = atoi(e);
     std::vector<LayerW> lw(m->cfg.n_layers);
     for (int l = 0; l < m->cfg.n_layers; ++l) {
         const LayerStore& L = m->layers[l];

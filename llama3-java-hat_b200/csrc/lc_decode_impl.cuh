@@ -180,6 +180,37 @@ __device__ __forceinline__ void run_producer(const DecodeParams& p, const Smem& 
     const int nlay = p.sched_n[2 * cta], ntot = nlay + p.sched_n[2 * cta + 1];
     uint32_t it = 0, slot = 0, par = 1;
     bool ok = true;
+    // L2 prefetch window (lane 0): cursor (ps, pi) at absolute tile Q runs up
+    // to D tiles ahead of the copies, also while the copy waits for a free
+    // stage, so HBM keeps streaming while the consumers wait for an exchange.
+    // The table entry of the next prefetch is loaded one call ahead.
+    const int D = p.l2_prefetch_tiles;
+    int ps = 0, pi = 0;
+    uint32_t Q = 0, pend = 0;
+    bool have = false;
+    auto pf_advance = [&]() {
+        ++Q;
+        if (++pi >= (lm_needed(p, p.pos0 + ps) ? ntot : nlay)) {
+            pi = 0;
+            ++ps;
+        }
+    };
+    auto pf_step = [&](uint32_t copied) {
+        if (D == 0) return;
+        while (Q < copied && ps < p.nsteps) {
+            pf_advance();
+            have = false;
+        }
+        if (ps >= p.nsteps || Q >= copied + (uint32_t)D) return;
+        if (!have) {
+            pend = __ldg(row + pi);
+            have = true;
+            return;
+        }
+        prefetch_l2(p.wbase + ((size_t)pend << 8), tb);
+        have = false;
+        pf_advance();
+    };
     for (int s = 0; s < p.nsteps && ok; ++s) {
         const int n = lm_needed(p, p.pos0 + s) ? ntot : nlay;
         uint32_t cur = lane < ntot ? __ldg(row + lane) : 0u;
@@ -195,6 +226,7 @@ __device__ __forceinline__ void run_producer(const DecodeParams& p, const Smem& 
                 if (!mbar_try_wait(&sm.empty[slot], par)) {
                     const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
                     for (uint32_t k = 1;; ++k) {
+                        pf_step(it);
                         if (mbar_try_wait(&sm.empty[slot], par)) break;
                         if ((k & 63u) == 0u) {
                             if (*stop != 0 || *err != 0) {
@@ -212,6 +244,7 @@ __device__ __forceinline__ void run_producer(const DecodeParams& p, const Smem& 
                 if (!fail) {
                     mbar_arrive_expect_tx(&sm.full[slot], tb);
                     bulk_g2s(sm.ring + (size_t)slot * tb, p.wbase + ((size_t)e << 8), tb, &sm.full[slot], policy);
+                    pf_step(it + 1);
                 }
             }
             if (__shfl_sync(0xffffffffu, fail, 0)) {
@@ -394,25 +427,44 @@ __device__ __forceinline__ bool gather_tagged(const DecodeParams& p, const uint6
             for (int j = 0; j < 4; ++j) fresh[k] = fresh[k] && (uint32_t)(w[k][j] >> 32) == want;
         }
     }
-    // Slow path (chunks not yet written): re-read, bounded.
-    bool ok = true;
+    // Slow path (chunks not yet written): re-read every stale chunk each
+    // round, all loads of a round in flight together; bounded.
+    bool stale = false;
 #pragma unroll
-    for (int k = 0; k < NV; ++k) {
-        if (!fresh[k]) {
-            const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
-            for (uint32_t it = 1;; ++it) {
-                __nanosleep(64);
-                if (ld_tag4(src + 4 * (size_t)idx[k], want, v[k])) break;
-                if ((it & 15u) == 0u &&
-                    (*reinterpret_cast<volatile int*>(p.err) != 0 || globaltimer_ns() > deadline)) {
-                    atomicCAS(p.err, 0, (int)kDevTimeoutGrid);
-                    ok = false;
-                    break;
+    for (int k = 0; k < NV; ++k) stale = stale || !fresh[k];
+    if (!stale) return true;
+    const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
+    for (uint32_t it = 1;; ++it) {
+        __nanosleep(128);
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            if (!fresh[k]) {
+                ld_word2(src + 4 * (size_t)idx[k], w[k][0], w[k][1]);
+                ld_word2(src + 4 * (size_t)idx[k] + 2, w[k][2], w[k][3]);
+            }
+        }
+        stale = false;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            if (!fresh[k]) {
+                bool f = true;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) f = f && (uint32_t)(w[k][j] >> 32) == want;
+                if (f) {
+                    v[k] = make_float4(__uint_as_float((uint32_t)w[k][0]), __uint_as_float((uint32_t)w[k][1]),
+                                       __uint_as_float((uint32_t)w[k][2]), __uint_as_float((uint32_t)w[k][3]));
+                    fresh[k] = true;
+                } else {
+                    stale = true;
                 }
             }
         }
+        if (!stale) return true;
+        if ((it & 15u) == 0u && (*reinterpret_cast<volatile int*>(p.err) != 0 || globaltimer_ns() > deadline)) {
+            atomicCAS(p.err, 0, (int)kDevTimeoutGrid);
+            return false;
+        }
     }
-    return ok;
 }
 
 // A set of CTAs whose exchange flags a reader waits for: with units > 0,
@@ -461,27 +513,29 @@ __device__ __forceinline__ bool wait_flags(const DecodeParams& p, uint32_t want,
         int n = f.units;
         if (n == 0)
             for (int k = 0; k < 3; ++k) n += f.rb[k] - f.ra[k];
-        const uint32_t* fp[kPollPerLane];
+        // CTA index of each flag this lane polls (all CTAs: lane + 32 k).
+        const bool all = f.units == G;
+        int c[kPollPerLane];
 #pragma unroll
         for (int k = 0; k < kPollPerLane; ++k) {
             const int i = lane + 32 * k;
-            int c = 0;
-            if (i < n) {
+            c[k] = 0;
+            if (!all && i < n) {
                 if (f.units > 0) {
-                    c = i * G / f.units;
+                    c[k] = i * G / f.units;
                 } else {
                     int j = i, q = 0;
                     while (q < 2 && j >= f.rb[q] - f.ra[q]) j -= f.rb[q] - f.ra[q++];
-                    c = (f.ra[q] + j - f.shift + G) % G;
+                    c[k] = (f.ra[q] + j - f.shift + G) % G;
                 }
             }
-            fp[k] = p.flags + c;
         }
         const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
         for (uint32_t it = 0;; ++it) {
             uint32_t v[kPollPerLane];
 #pragma unroll
-            for (int k = 0; k < kPollPerLane; ++k) v[k] = lane + 32 * k < n ? ld_flag(fp[k]) : want;
+            for (int k = 0; k < kPollPerLane; ++k)
+                v[k] = lane + 32 * k < n ? ld_flag(p.flags + (all ? lane + 32 * k : c[k])) : want;
             bool mine = true;
 #pragma unroll
             for (int k = 0; k < kPollPerLane; ++k) mine &= (v[k] - want) < 0x80000000u;
@@ -544,9 +598,9 @@ __device__ __forceinline__ bool stage_norm(const DecodeParams& p, const Smem& sm
     }
     bool ok = true;
     if (src) {
-        ok = wait_flags(p, want, all_ctas());
+        // The tagged words are polled directly: no flag round trip.
         tr.mark();
-        ok = gather_tagged<2>(p, src, idx, want, xv) && ok;
+        ok = gather_tagged<2>(p, src, idx, want, xv);
         tr.mark();
     } else {
         tr.mark();
@@ -598,7 +652,7 @@ __device__ __forceinline__ bool stage_norm(const DecodeParams& p, const Smem& sm
 __device__ __forceinline__ bool stage_att(const DecodeParams& p, const Smem& sm, int nsplit, uint32_t want,
                                           Tracer& tr) {
     constexpr int HD = kAttnHeadDim;
-    bool ok = wait_flags(p, want, attn_ctas(p, nsplit));
+    bool ok = true;  // tagged words, polled directly
     tr.mark();
     const int tid = threadIdx.x, qdim = p.n_heads * HD;
     float4 v[2];
@@ -775,7 +829,7 @@ struct RingPos {
 // Out of line: the hot loop gets a register allocation of its own, with
 // nothing of the caller's state live in it.
 template <int KS>
-__device__ __noinline__ RingPos consume_batch(const DecodeParams& p, RingPos r, int b0, int b1, int ncb, bool timing) {
+__device__ __forceinline__ RingPos consume_batch(const DecodeParams& p, RingPos r, int b0, int b1, int ncb, bool timing) {
     const Smem sm = smem_view<KS>();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, ng = b1 - b0;
     const uint32_t ring = smem_u32(sm.ring);
@@ -873,9 +927,9 @@ __device__ __forceinline__ bool consume_job(const DecodeParams& p, const Smem& s
 __device__ __forceinline__ bool attn_unit(const DecodeParams& p, int s, int l, int pos, int kvh, int t0, int t1,
                                           int nsplit, int sp, int qkv_shift, float* sm, Tracer& tr) {
     constexpr int HD = kAttnHeadDim, VPT = kVChunk * HD / 4 / kCT;  // float4 of a chunk per thread
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, G = gridDim.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kv_mul = p.n_heads / p.n_kv, T = t1 - t0, pr = pos - t0;  // pr: row of pos in the unit
-    const int qdim = p.n_heads * HD, kvd = p.n_kv * HD;
+    const int kvd = p.n_kv * HD;
     const uint32_t in_tag = xtag(p, s, 5 * l + 0), out_tag = xtag(p, s, 5 * l + 1);
     float* qs = sm;
     float* cur = qs + kv_mul * HD;  // this position's k, v
@@ -908,21 +962,8 @@ __device__ __forceinline__ bool attn_unit(const DecodeParams& p, int s, int l, i
             reinterpret_cast<float4*>(kvs)[(pr - c0) * (HD / 4) + tid] =
                 reinterpret_cast<const float4*>(cur + which * HD)[tid];
     };
-    load_rows(K4, 0, 32);  // warp 0 starts polling at once
-    // Owners of q rows (heads of this kv head), k rows and v rows of kvh.
-    FlagSet f;
-    f.units = 0;
-    f.shift = qkv_shift;
-    {
-        const int P = (qdim + 2 * kvd) / 8;
-        const int ga[3] = {kvh * kv_mul * HD / 8, (qdim + kvh * HD) / 8, (qdim + kvd + kvh * HD) / 8};
-        const int gn[3] = {kv_mul * HD / 8, HD / 8, HD / 8};
-        for (int k = 0; k < 3; ++k) {
-            f.ra[k] = owner_rank(P, G, ga[k]);
-            f.rb[k] = owner_rank(P, G, ga[k] + gn[k] - 1) + 1;
-        }
-    }
-    bool ok = wait_flags(p, in_tag, f);
+    load_rows(K4, 0, 32);  // warp 0 starts on q / k / v at once
+    bool ok = true;
     tr.mark();
     // q and this position's k, v (tagged), one float4 per thread; the first
     // V chunk (cache rows) in registers meanwhile.

@@ -136,6 +136,8 @@ struct DecodeParams {
     const int* sched_n;
     int sched_stride;
     const uint8_t* wbase;
+    // L2 prefetch window of the producer, in tiles ahead of the copies (0: off).
+    int l2_prefetch_tiles;
 };
 
 struct DecodeLaunch {

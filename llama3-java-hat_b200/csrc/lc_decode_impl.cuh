@@ -24,12 +24,18 @@
 // of mma.sync m16n8k16 with fp32 accumulation.  Per-warp partial sums meet in
 // shared memory and the job epilogue adds them in a fixed order.
 //
-// Exchanges: a CTA raises its flag word to a monotonically increasing tag
-// after its stores for an exchange; a reader's warp 0 polls all flags, then
-// the CTA reads the data from L2.  Every wait is bounded: a timeout records an
-// error code in p.err, every later wait returns at once, all CTAs leave at
-// the next step boundary, the producer drains its in-flight copies, and the
-// host reports LC_ERR_TIMEOUT.
+// Exchanges: x (after O and DN), q, this position's k and v, the attention
+// outputs and partials and the argmax candidates travel as 64-bit words
+// {fp32 bits, tag}, the tag unique per (launch, position, exchange); readers
+// poll the words themselves until every one carries the wanted tag, so one
+// L2 round trip brings data and completion together.  h (the gate/up output,
+// the widest vector) stays plain fp32: writers fence, then raise a per-CTA
+// flag word to the tag, and readers wait for all flags with acquire.  The end
+// of a position is a fenced flag exchange, which orders the plain KV-cache
+// stores before every later position.  Every wait is bounded: a timeout
+// records an error code in p.err, every later wait returns at once, all CTAs
+// leave at the next step boundary, the producer drains its in-flight copies,
+// and the host reports LC_ERR_TIMEOUT.
 #pragma once
 // Included by lc_decode.cu (LC_DECODE_TRACE 0) and lc_decode_trace.cu
 // (LC_DECODE_TRACE 1, the phase-trace build of the same kernel).

@@ -80,6 +80,22 @@ int lc_gemv_f32(lc_context* ctx, const float* W, const float* x, float* y, int r
 int lc_gemv_f16_batched(lc_context* ctx, const uint16_t* W, const float* X, float* Y, int rows, int cols,
                         int batch);
 
+/* Row-major F16 W [rows][cols] (host or device) -> Wt in the tiled layout the
+ * tensor-core product reads: 8-row tiles of `w` columns (w = the largest
+ * multiple of 64 up to 2048 dividing cols), [w/8 octets][8 rows][8 halves]
+ * per tile.  rows % 8 == 0, cols % 64 == 0.  No reference counterpart (the
+ * reference keeps W row-major: F16Weights, H/F16Weights.java:18-27). */
+int lc_weights_tile(lc_context* ctx, const uint16_t* W, uint16_t* Wt, int rows, int cols);
+
+/* The IGEMV product (K/IGEMV.java:34-68, sequential fp32 sums of
+ * K/GEMV.java:66-91) for `batch` activation rows at once on the tcgen05
+ * tensor cores: Y[b][r] = sum_c W[r][c] * X[b][c].  Wt: device memory from
+ * lc_weights_tile; X [batch][cols], Y [batch][rows] fp32, host or device.
+ * batch 1..64, rows % 16 == 0, cols % 64 == 0.  Each X row is split into
+ * f16 hi + lo parts under a power-of-two row scale (2^-22 relative), the
+ * products are exact and accumulate in fp32. */
+int lc_gemm_f16_tiled(lc_context* ctx, const uint16_t* Wt, const float* X, float* Y, int rows, int cols, int batch);
+
 /* IRMSNorm.apply(x, weight, size) K/IRMSNorm.java:17; K/RMSNorm.java:35-50.
  * In place, eps = 1e-5f (K/RMSNorm.java:22). */
 int lc_rmsnorm(lc_context* ctx, float* x, const float* weight, int size);

@@ -75,6 +75,9 @@ struct lc_context {
     int* d_err = nullptr;           // device error word of standalone kernels
     void* attn_scratch = nullptr;
     size_t attn_scratch_bytes = 0;
+    void* gemm_scratch = nullptr;   // row maxima, N-block tickets (zeroed), partial sums
+    size_t gemm_scratch_bytes = 0;
+    bool gemm_ready = false;        // shared-memory attribute of the GEMM kernel set
 };
 
 extern "C" int lc_device_count(int* count) {
@@ -112,6 +115,7 @@ extern "C" int lc_context_destroy(lc_context* c) {
     cudaStreamSynchronize(c->stream);
     for (void* p : c->pool) cudaFree(p);
     if (c->attn_scratch) cudaFree(c->attn_scratch);
+    if (c->gemm_scratch) cudaFree(c->gemm_scratch);
     if (c->d_err) cudaFree(c->d_err);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -296,6 +300,71 @@ extern "C" int lc_gemv_f16_batched(lc_context* c, const uint16_t* W, const float
     if (s.status != LC_OK) return s.status;
     launch_gemv_batched_f16(dW, dX, dY, rows, cols, batch, c->stream);
     return s.finish(cudaGetLastError());
+}
+
+// Tensor-core batched product on tiled weights (lc_gemm.cu).
+extern "C" int lc_weights_tile(lc_context* c, const uint16_t* W, uint16_t* Wt, int rows, int cols) {
+    CTX_CHECK(c);
+    if (rows <= 0 || cols <= 0 || rows % 8 || gemm_tile_width(cols) == 0)
+        return fail(LC_ERR_INVALID_ARG, "rows=%d cols=%d (rows %% 8 == 0 and cols %% 64 == 0 required)", rows, cols);
+    Stager s(c);
+    auto* dW = (const __half*)s.arg(W, (size_t)rows * cols * 2, kIn);
+    auto* dT = (__half*)s.arg(Wt, (size_t)rows * cols * 2, kOut);
+    if (s.status != LC_OK) return s.status;
+    if (((uintptr_t)dW | (uintptr_t)dT) & 15) return fail(LC_ERR_INVALID_ARG, "W and Wt must be 16-byte aligned");
+    return s.finish(launch_tile_rows(dW, dT, rows, cols, gemm_tile_width(cols), 0, 1, c->stream));
+}
+
+extern "C" int lc_gemm_f16_tiled(lc_context* c, const uint16_t* Wt, const float* X, float* Y, int rows, int cols,
+                                 int batch) {
+    CTX_CHECK(c);
+    if (rows <= 0 || cols <= 0 || batch <= 0 || batch > kGemmMaxB || rows % 16 || gemm_tile_width(cols) == 0)
+        return fail(LC_ERR_INVALID_ARG, "rows=%d cols=%d batch=%d (rows %% 16 == 0, cols %% 64 == 0, batch 1..%d)",
+                    rows, cols, batch, kGemmMaxB);
+    GemmParams g;
+    memset(&g, 0, sizeof(g));
+    g.N = rows;
+    g.K = cols;
+    g.cbw = gemm_tile_width(cols);
+    g.lda = cols;
+    g.B = batch;
+    if (!gemm_plan(&g, c->sms)) return fail(LC_ERR_INVALID_ARG, "unsupported GEMM shape %d x %d", rows, cols);
+    Stager s(c);
+    auto* dW = (const __half*)s.arg(Wt, (size_t)rows * cols * 2, kIn);
+    auto* dX = (const float*)s.arg(X, (size_t)batch * cols * 4, kIn);
+    auto* dY = (float*)s.arg(Y, (size_t)batch * rows * 4, kOut);
+    if (s.status != LC_OK) return s.status;
+    if (((uintptr_t)dW | (uintptr_t)dX | (uintptr_t)dY) & 15) return fail(LC_ERR_INVALID_ARG, "buffers must be 16-byte aligned");
+    const size_t nbk = (size_t)(rows + g.nblk - 1) / g.nblk;
+    const size_t off_t = 256, off_p = off_t + ((nbk * 4 + 255) / 256) * 256;
+    const size_t need = off_p + gemm_part_bytes(g);
+    if (c->gemm_scratch_bytes < need) {
+        if (c->gemm_scratch) cudaFree(c->gemm_scratch);
+        c->gemm_scratch = nullptr;
+        c->gemm_scratch_bytes = 0;
+        CK(cudaMalloc(&c->gemm_scratch, need), "GEMM scratch");
+        CK(cudaMemset(c->gemm_scratch, 0, need), "GEMM scratch");
+        c->gemm_scratch_bytes = need;
+    }
+    if (!c->gemm_ready) {
+        CK(gemm_prepare(), "GEMM shared-memory attribute");
+        c->gemm_ready = true;
+    }
+    uint8_t* base = (uint8_t*)c->gemm_scratch;
+    float* rowmax = (float*)base;
+    g.W = dW;
+    g.A = dX;
+    g.rowmax = rowmax;
+    g.tickets = (uint32_t*)(base + off_t);
+    g.part = (float*)(base + off_p);
+    g.op = kGemmStore;
+    g.y = dY;
+    g.ldy = rows;
+    g.err = c->d_err;
+    g.timeout_ns = 2000000000ull;
+    cudaError_t e = launch_rowmax(dX, cols, cols, batch, rowmax, c->stream);
+    if (e == cudaSuccess) e = launch_gemm(g, c->sms, c->stream);
+    return s.finish(e);
 }
 
 extern "C" int lc_rmsnorm_rows(lc_context* c, float* x, const float* w, int rows, int width, float eps) {

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstring>
 #include <vector>
 
 #include "lc_common.cuh"
@@ -165,5 +166,80 @@ cudaError_t launch_decode(const DecodeParams& p, const DecodeLaunch& l, cudaStre
 // Same kernel built with the phase trace (p.trace must be set).
 cudaError_t decode_prepare_traced(const DecodeLaunch& l);
 cudaError_t launch_decode_traced(const DecodeParams& p, const DecodeLaunch& l, cudaStream_t st);
+
+// ---- batched GEMM on tcgen05 (lc_gemm.cu) ----
+//
+// Y[s][n] = sum_k A[s][k] * W[n][k] for B <= 64 activation rows, W F16 in the
+// tiled layout above (column-block width cbw), A fp32 with rowmax[s] =
+// max_k |A[s][k]| supplied (the power-of-two scale of the hi / lo split).
+// The result goes through one of the fused epilogues.
+enum GemmOp : int {
+    kGemmStore = 0,   // y[s * ldy + n] = v
+    kGemmResid = 1,   // y[s * ldy + n] += v (residual add, in place)
+    kGemmQKV = 2,     // RoPE on q and k, q -> q[s][n], k / v -> the KV cache at pos[s]
+    kGemmSwiGLU = 3,  // rows 4m..4m+3 = (gate, up) pairs: h[s][2m + j] = silu(g) * u; hmax[s] = max |h|
+    kGemmLogits = 4,  // logits[s][n] (optional) and best[s] = packed (value, lowest index) argmax
+};
+
+constexpr int kGemmMaxB = 64;
+constexpr int kGemmHeadDim = 64;  // head_dim of the kGemmQKV epilogue
+
+struct GemmParams {
+    const __half* W;  // tiled
+    int N, K, cbw;    // rows, columns, column-block width (K % cbw == 0, cbw % 64 == 0)
+    const float* A;   // [B][lda]
+    int lda, B;
+    const float* rowmax;  // [B]
+    int nblk, kspl, units;   // N-block rows, K splits, (N-blocks) * kspl
+    float* part;             // [kspl][B][N] partial sums when kspl > 1
+    uint32_t* tickets;       // [N-blocks], zero between launches, when kspl > 1
+    int op;
+    float* y;
+    int ldy;
+    // kGemmQKV
+    float* q;
+    int qdim, kvd;
+    float* kcache;
+    float* vcache;            // this layer's base: + s * kv_seq_stride + head * kv_head_stride + pos * 64
+    int64_t kv_seq_stride, kv_head_stride;
+    const int32_t* pos;       // [B]
+    const float* rope_freq;   // [head_dim / 2]
+    // kGemmSwiGLU
+    float* h;
+    int ldh;
+    uint32_t* hmax;           // [B] float bits of max |h|, atomicMax
+    // kGemmLogits
+    float* logits;
+    int ldl;
+    unsigned long long* best; // [B]
+    int* err;
+    uint64_t timeout_ns;
+};
+
+// Chooses nblk and kspl for a grid of `num_sms` CTAs; fills units.  Returns
+// false when the shape is unsupported (N % 16, K % 64, K % cbw, B range).
+bool gemm_plan(GemmParams* p, int num_sms);
+// Bytes of the partial-sum buffer p needs (0 when kspl == 1).
+size_t gemm_part_bytes(const GemmParams& p);
+cudaError_t gemm_prepare();  // sets the shared-memory attribute once
+cudaError_t launch_gemm(const GemmParams& p, int num_sms, cudaStream_t st);
+// rowmax[s] = max |A[s][0..K)| (float bits) for the standalone entry point.
+cudaError_t launch_rowmax(const float* A, int lda, int K, int B, float* rowmax, cudaStream_t st);
+// Row-major F16 [rows][cols] -> tiled layout with column-block width cbw.
+int gemm_tile_width(int cols);
+
+// Argmax key: order-preserving float bits above the inverted index, so the
+// largest key is the largest value with the lowest index.
+__host__ __device__ inline unsigned long long argmax_key(float v, int idx) {
+#ifdef __CUDA_ARCH__
+    uint32_t b = __float_as_uint(v);
+#else
+    uint32_t b;
+    memcpy(&b, &v, 4);
+#endif
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)b << 32) | (uint32_t)(~(uint32_t)idx);
+}
+__host__ __device__ inline int argmax_key_index(unsigned long long k) { return (int)(~(uint32_t)(k & 0xffffffffu)); }
 
 }  // namespace lc

@@ -1,0 +1,94 @@
+// lc_tcgen05.cuh -- PTX wrappers for the 5th-generation tensor cores of
+// sm_100a: tensor-memory (TMEM) allocation, tcgen05.mma with shared-memory
+// operand descriptors, completion through mbarriers, TMEM loads, and the
+// fences that order tcgen05 work against thread synchronisation.
+//
+// Operand layout used throughout: K-major, no swizzle.  A "core matrix" is 8
+// rows x 16 bytes (8 halves) stored as 128 contiguous bytes; the core
+// matrices of one operand tile sit 128 B apart along K (leading byte offset)
+// and 1024 B apart along M / N (stride byte offset), i.e. a tile of R rows x
+// 64 columns is [R/8 row groups][8 column octets][8 rows][8 halves].  This is
+// exactly the order of the tiled weight layout (lc_internal.h), so weight
+// tiles reach shared memory with plain 1-D bulk copies.
+#pragma once
+
+#include "lc_common.cuh"
+
+namespace lc {
+
+// Shared-memory matrix descriptor (tcgen05 "matrix descriptor"): start
+// address >> 4 in bits 0-13, leading byte offset >> 4 in 16-29, stride byte
+// offset >> 4 in 32-45, descriptor version 1 in bits 46-47, base offset 0,
+// absolute leading-offset mode 0, layout type 0 (no swizzle) in bits 61-63.
+LC_DEV uint64_t tc_desc_kmajor(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+
+// Instruction descriptor of kind::f16 with f16 A and B (formats 0), fp32
+// accumulation (D format 1, bits 4-5), both operands K-major (bits 15, 16 =
+// 0), N >> 3 in bits 17-22 and M >> 4 in bits 24-28.
+__host__ __device__ constexpr uint32_t tc_idesc_f16_f32(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// TMEM allocation by one full warp: the base address is written to *slot.
+// ncols is a power of two >= 32.
+LC_DEV void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+LC_DEV void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
+
+LC_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+LC_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+LC_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Generic-proxy shared-memory writes become visible to the tensor cores
+// (async proxy) after this fence and a synchronisation.
+LC_DEV void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// D[tmem] (+)= A[adesc] * B[bdesc]^T, one thread issues; accumulate != 0
+// adds to D, 0 overwrites it.
+LC_DEV void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// The mbarrier receives one arrival when every tcgen05 operation this thread
+// issued before has completed.
+LC_DEV void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 16 consecutive 32-bit columns of the warp's 32 TMEM lanes (thread i: lane
+// base + i).  The values are valid after tmem_wait_ld, which takes them as
+// operands so no use can be scheduled before it.
+LC_DEV void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+
+LC_DEV void tmem_wait_ld(uint32_t (&v)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]),
+                   "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]),
+                   "+r"(v[15])
+                 :
+                 : "memory");
+}
+
+}  // namespace lc

@@ -79,6 +79,8 @@ SIGNATURES = {
     "lc_gemv_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]),
     "lc_gemv_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]),
     "lc_gemv_f16_batched": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int]),
+    "lc_weights_tile": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int]),
+    "lc_gemm_f16_tiled": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int]),
     "lc_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int]),
     "lc_rmsnorm_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float]),
     "lc_rope": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_float]),

@@ -196,6 +196,20 @@ class CudaGEMV(_CudaKernel, IGEMV):
                                                 _addr(X, "f32", batch * cols),
                                                 _addr(Y, "f32", batch * rows, writable=True), rows, cols, batch))
 
+    def tile(self, matrix, tiled, rows: int, cols: int) -> None:
+        """Row-major F16 matrix -> the tiled layout of the tensor-core product
+        (`tiled`: device memory, rows * cols halves)."""
+        n = rows * cols
+        _lib.check(self.lib.lc_weights_tile(self.ctx, _addr(matrix, "f16", n), _addr(tiled, "f16", n, writable=True),
+                                            rows, cols))
+
+    def apply_batched_tiled(self, tiled, X, Y, rows: int, cols: int, batch: int) -> None:
+        """Y[b] = W @ X[b] for b < batch <= 64 on the tcgen05 tensor cores; W
+        given in the tiled layout (`tile`)."""
+        _lib.check(self.lib.lc_gemm_f16_tiled(self.ctx, _addr(tiled, "f16", rows * cols),
+                                              _addr(X, "f32", batch * cols),
+                                              _addr(Y, "f32", batch * rows, writable=True), rows, cols, batch))
+
 
 class CudaRMSNorm(_CudaKernel, IRMSNorm):
     """RMSNorm.java:35-50 on the GPU: one fused reduce + normalise kernel."""

@@ -326,7 +326,6 @@ extern "C" int lc_gemm_f16_tiled(lc_context* c, const uint16_t* Wt, const float*
     g.N = rows;
     g.K = cols;
     g.cbw = gemm_tile_width(cols);
-    g.lda = cols;
     g.B = batch;
     if (!gemm_plan(&g, c->sms)) return fail(LC_ERR_INVALID_ARG, "unsupported GEMM shape %d x %d", rows, cols);
     Stager s(c);
@@ -336,7 +335,8 @@ extern "C" int lc_gemm_f16_tiled(lc_context* c, const uint16_t* Wt, const float*
     if (s.status != LC_OK) return s.status;
     if (((uintptr_t)dW | (uintptr_t)dX | (uintptr_t)dY) & 15) return fail(LC_ERR_INVALID_ARG, "buffers must be 16-byte aligned");
     const size_t nbk = (size_t)(rows + g.nblk - 1) / g.nblk;
-    const size_t off_t = 256, off_p = off_t + ((nbk * 4 + 255) / 256) * 256;
+    const size_t off_t = 256, off_a = off_t + ((nbk * 4 + 255) / 256) * 256;
+    const size_t off_p = off_a + ((gemm_split_bytes(batch, cols) + 255) / 256) * 256;
     const size_t need = off_p + gemm_part_bytes(g);
     if (c->gemm_scratch_bytes < need) {
         if (c->gemm_scratch) cudaFree(c->gemm_scratch);
@@ -351,10 +351,11 @@ extern "C" int lc_gemm_f16_tiled(lc_context* c, const uint16_t* Wt, const float*
         c->gemm_ready = true;
     }
     uint8_t* base = (uint8_t*)c->gemm_scratch;
-    float* rowmax = (float*)base;
+    float* unscale = (float*)base;
+    uint8_t* As = base + off_a;
     g.W = dW;
-    g.A = dX;
-    g.rowmax = rowmax;
+    g.As = As;
+    g.unscale = unscale;
     g.tickets = (uint32_t*)(base + off_t);
     g.part = (float*)(base + off_p);
     g.op = kGemmStore;
@@ -362,8 +363,11 @@ extern "C" int lc_gemm_f16_tiled(lc_context* c, const uint16_t* Wt, const float*
     g.ldy = rows;
     g.err = c->d_err;
     g.timeout_ns = 2000000000ull;
-    cudaError_t e = launch_rowmax(dX, cols, cols, batch, rowmax, c->stream);
-    if (e == cudaSuccess) e = launch_gemm(g, c->sms, c->stream);
+    CUtensorMap wmap, amap;
+    if (gemm_make_wmap(&wmap, g) != cudaSuccess || gemm_make_amap(&amap, g) != cudaSuccess)
+        return fail(LC_ERR_CUDA, "tensor map encoding failed");
+    cudaError_t e = launch_gemm_split(dX, cols, cols, batch, As, unscale, c->stream);
+    if (e == cudaSuccess) e = launch_gemm(g, wmap, amap, c->sms, c->stream);
     return s.finish(e);
 }
 

@@ -92,6 +92,13 @@ LC_DEV uint64_t l2_policy_evict_first() {
     return p;
 }
 
+// L2 policy for data every CTA reads again (batched activations).
+LC_DEV uint64_t l2_policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 // 1-D bulk copy global -> this CTA's shared memory, completion signalled as
 // transaction bytes on `bar`.  dst, src and bytes must be multiples of 16.
 LC_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {

@@ -15,50 +15,53 @@
 // warp: a shuffle).  Products of f16 values are exact; accumulation is fp32.
 //
 // Work unit = (N block of nblk rows, K split).  Units are dealt round-robin
-// over a grid of at most one CTA per SM.  Warp roles (320 threads):
-//   warp 0     streams the unit's weight blocks: per 64-column chunk and
-//              8-row tile one 1 KB 1-D bulk copy (the tile's 8 octets of the
-//              chunk are contiguous in the tiled layout) into a 4-stage ring;
+// over a grid of at most one CTA per SM.  A is split once per product
+// (launch_gemm_split, or fused into the producing kernel) into the MMA's
+// K-major layout in global memory, so both operands reach shared memory as
+// 1-D bulk copies.  Warp roles (192 threads):
+//   warp 0     lane 0, per 64-column chunk: one TMA box of the weights (a 4-D
+//              tensor map over the tiled layout: 8 octets x nblk/8 tiles,
+//              landing in the MMA's K-major core-matrix order) and one box
+//              of the pre-split activations (3-D map), into a ring of 4..12
+//              stages (fewer, larger stages for wide N blocks: about 190 KB
+//              in flight);
 //   warp 1     allocates 512 TMEM columns (two 256-column accumulators);
-//              lane 0 issues the MMAs of each chunk and commits them to the
+//              lane 0 issues the MMAs of each chunk, commits them to the
 //              stage's "empty" barrier, and each unit to its accumulator;
-//   warps 2-5  epilogue: TMEM lane quarter warp % 4, 16 columns per load;
-//   warps 6-9  load the unit's A chunks (fp32, L2) and write hi / lo in the
-//              canonical K-major layout, then arrive on the stage.
+//   warps 2-5  epilogue: TMEM lane quarter warp % 4, 16 columns per load.
 // With kspl > 1 every unit writes its partial sums; the last unit of an N
 // block (ticket) adds them in split order (deterministic) and runs the
 // epilogue.  Every wait is bounded (error word + LC_ERR_TIMEOUT); TMEM is
 // released and in-flight copies and MMAs are drained on every path.
+#include <cudaTypedefs.h>
+
 #include "lc_internal.h"
 #include "lc_tcgen05.cuh"
 
 namespace lc {
 namespace {
 
-constexpr int kThreads = 320;
-constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kMaxStages = 12;
+constexpr int kRingBytes = 200 * 1024;
 constexpr int kKC = 64;                   // columns per stage
-constexpr int kABytes = 128 * kKC * 2;    // 16 KB: 128 MMA rows
+constexpr int kABytes = 128 * kKC * 2;    // 16 KB: 128 MMA rows (only the used row groups are copied)
 constexpr int kMaxN = 256;
-constexpr int kWBytes = kMaxN * kKC * 2;  // 32 KB
-constexpr int kStageBytes = kABytes + kWBytes;
 constexpr int kTmemCols = 512;
 constexpr uint32_t kBarEpi = 1;           // named barrier of the 128 epilogue threads
-constexpr int kEpiT0 = 64, kLoadT0 = 192; // first thread of the epilogue / loader warps
+constexpr int kEpiT0 = 64;                // first epilogue thread
 
 struct Bars {
-    uint64_t wfull[kStages];  // weight bytes landed (producer arrive + tx)
-    uint64_t afull[kStages];  // A chunk written (4 loader warps)
-    uint64_t empty[kStages];  // MMAs of the stage done (tcgen05.commit)
+    uint64_t full[kMaxStages];   // weight and activation bytes landed (producer arrive + tx)
+    uint64_t empty[kMaxStages];  // MMAs of the stage done (tcgen05.commit)
     uint64_t dfull[2];        // accumulator complete (tcgen05.commit)
     uint64_t dempty[2];       // accumulator read out (epilogue)
     uint64_t drain;           // all MMAs of the CTA done
     uint32_t tmem;
     int flag;
-    uint32_t rmax[kGemmMaxB];
     unsigned long long best[kGemmMaxB];
 };
-constexpr int kSmemBytes = kStages * kStageBytes + (int)sizeof(Bars);
+constexpr int kSmemMax = kRingBytes + (int)sizeof(Bars);
 
 // Row scale of the hi / lo split (same rule as the fused decode kernel).
 __device__ __forceinline__ int row_exp(float m) {
@@ -124,8 +127,6 @@ __device__ __forceinline__ void apply4(const GemmParams& p, Bars* bs, int s, int
             const float h0 = __fmul_rn(silu_ref(y[0]), y[1]);
             const float h1 = __fmul_rn(silu_ref(y[2]), y[3]);
             *reinterpret_cast<float2*>(p.h + (size_t)s * p.ldh + (n >> 1)) = make_float2(h0, h1);
-            const float m = fmaxf(fabsf(h0), fabsf(h1));
-            if (m > 0.0f) atomicMax(&bs->rmax[s], __float_as_uint(m));
             break;
         }
         default: {  // kGemmLogits
@@ -152,16 +153,18 @@ __device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t par, const Gem
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ GemmParams p,
+                                                           const __grid_constant__ CUtensorMap wmap,
+                                                           const __grid_constant__ CUtensorMap amap) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    Bars* bs = reinterpret_cast<Bars*>(smem + kStages * kStageBytes);
+    const int NS = p.stages, SB = p.stage_bytes;
+    Bars* bs = reinterpret_cast<Bars*>(smem + NS * SB);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = gridDim.x;
-    const int krange = p.K / p.kspl, nchunk = krange / kKC, ncb = p.K / p.cbw;
+    const int krange = p.K / p.kspl, nchunk = krange / kKC, ncb = p.K / p.cbw, nrg = (p.B + 3) >> 2;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&bs->wfull[s], 1);
-            mbar_init(&bs->afull[s], 4);
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&bs->full[s], 1);
             mbar_init(&bs->empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -181,67 +184,71 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const uint32_t tmem = bs->tmem;
 
     if (warp == 0) {
-        // ---------------------------------------------------- weight stream --
-        const uint64_t policy = l2_policy_evict_first();
-        uint32_t it = 0;
-        bool ok = true;
-        for (int u = blockIdx.x; u < p.units && ok; u += G) {
-            const int nbi = u / p.kspl, ks = u % p.kspl, n0 = nbi * p.nblk;
-            const int ntile = min(p.nblk, p.N - n0) >> 3;
-            for (int c = 0; c < nchunk; ++c, ++it) {
-                const uint32_t slot = it % kStages, par = ((it / kStages) & 1u) ^ 1u;
-                if (!wait_warp(&bs->empty[slot], par, p, kDevTimeoutEmpty)) {
-                    ok = false;
-                    break;
-                }
-                const int kc = ks * krange + c * kKC, cb = kc / p.cbw, o0 = (kc % p.cbw) >> 3;
-                if (lane == 0) mbar_arrive_expect_tx(&bs->wfull[slot], (uint32_t)ntile * 1024u);
-                __syncwarp();
-                uint8_t* dst = smem + slot * kStageBytes + kABytes;
-                for (int t = lane; t < ntile; t += 32) {
-                    const __half* src = p.W + (((size_t)(n0 >> 3) + t) * ncb + cb) * (size_t)(8 * p.cbw) + o0 * 64;
-                    bulk_g2s(dst + t * 1024, src, 1024u, &bs->wfull[slot], policy);
+        // ------------------------------------------------------ copy stream --
+        if (lane == 0) {
+            const uint64_t wpol = l2_policy_evict_first(), apol = l2_policy_evict_last();
+            const uint32_t tx = (uint32_t)(p.nblk * kKC * 2 + nrg * 1024);  // full boxes, out-of-range rows zero-filled
+            uint32_t it = 0, slot = 0, par = 1;
+            bool ok = true;
+            for (int u = blockIdx.x; u < p.units && ok; u += G) {
+                const int ks = u % p.kspl, g0 = ((u / p.kspl) * p.nblk) >> 3;
+                for (int c = 0; c < nchunk; ++c) {
+                    if (!mbar_wait_bounded(&bs->empty[slot], par, p.err, globaltimer_ns() + p.timeout_ns,
+                                           kDevTimeoutEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    const int kc = ks * krange + c * kKC;
+                    uint8_t* st = smem + slot * SB;
+                    mbar_arrive_expect_tx(&bs->full[slot], tx);
+                    tma_load_4d(st + kABytes, &wmap, 0, (kc % p.cbw) >> 3, kc / p.cbw, g0, &bs->full[slot], wpol);
+                    tma_load_3d(st, &amap, 0, kc >> 3, 0, &bs->full[slot], apol);
+                    ++it;
+                    if (++slot == (uint32_t)NS) {
+                        slot = 0;
+                        par ^= 1u;
+                    }
                 }
             }
-        }
-        // Every issued copy lands before the CTA may exit.
-        if (lane == 0) {
-            const uint32_t first = it > (uint32_t)kStages ? it - kStages : 0u;
+            // Every issued copy lands before the CTA may exit.
+            const uint32_t first = it > (uint32_t)NS ? it - NS : 0u;
             for (uint32_t k = first; k < it; ++k)
-                mbar_wait_bounded(&bs->wfull[k % kStages], (k / kStages) & 1u, p.err, globaltimer_ns() + 200000000ull,
+                mbar_wait_bounded(&bs->full[k % NS], (k / NS) & 1u, p.err, globaltimer_ns() + 200000000ull,
                                   kDevTimeoutDrain);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------- MMA --
         if (lane == 0) {
-            uint32_t it = 0;
+            uint32_t slot = 0, par = 0;
             int j = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < p.units && ok; u += G, ++j) {
                 const int a = j & 1, n0 = (u / p.kspl) * p.nblk, nb = min(p.nblk, p.N - n0);
-                if (!mbar_wait_bounded(&bs->dempty[a], ((j >> 1) & 1) ^ 1, p.err,
-                                       globaltimer_ns() + p.timeout_ns, kDevTimeoutFull)) {
+                if (!mbar_wait_bounded(&bs->dempty[a], ((j >> 1) & 1) ^ 1, p.err, globaltimer_ns() + p.timeout_ns,
+                                       kDevTimeoutFull)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(a * kMaxN);
                 const uint32_t idesc = tc_idesc_f16_f32(128, nb);
-                for (int c = 0; c < nchunk; ++c, ++it) {
-                    const uint32_t slot = it % kStages, par = (it / kStages) & 1u;
-                    const uint64_t dl = globaltimer_ns() + p.timeout_ns;
-                    if (!mbar_wait_bounded(&bs->wfull[slot], par, p.err, dl, kDevTimeoutFull) ||
-                        !mbar_wait_bounded(&bs->afull[slot], par, p.err, dl, kDevTimeoutFull)) {
+                for (int c = 0; c < nchunk; ++c) {
+                    if (!mbar_wait_bounded(&bs->full[slot], par, p.err, globaltimer_ns() + p.timeout_ns,
+                                           kDevTimeoutFull)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t ab = smem_u32(smem + slot * kStageBytes), wb = ab + kABytes;
+                    const uint32_t ab = smem_u32(smem + slot * SB), wb = ab + kABytes;
 #pragma unroll
                     for (int k = 0; k < kKC / 16; ++k)
                         tc_mma_f16(d, tc_desc_kmajor(ab + k * 256, 128, 1024), tc_desc_kmajor(wb + k * 256, 128, 1024),
                                    idesc, (c | k) != 0 ? 1u : 0u);
                     tc_commit(&bs->empty[slot]);
+                    if (++slot == (uint32_t)NS) {
+                        slot = 0;
+                        par ^= 1u;
+                    }
                 }
                 if (ok) tc_commit(&bs->dfull[a]);
             }
@@ -249,18 +256,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             tc_commit(&bs->drain);
             mbar_wait_bounded(&bs->drain, 0, p.err, globaltimer_ns() + 200000000ull, kDevTimeoutDrain);
         }
-    } else if (warp < 6) {
+    } else {
         // -------------------------------------------------------- epilogue --
         const int et = threadIdx.x - kEpiT0, q4 = warp & 3, r = q4 * 32 + lane, s = r >> 1;
         const bool lead = (r & 1) == 0 && s < p.B;
-        const float unscale = s < p.B ? __int_as_float((127 - row_exp(__ldg(p.rowmax + s))) << 23) : 0.0f;
+        const float unscale = s < p.B ? __ldg(p.unscale + s) : 0.0f;
         int j = 0;
         for (int u = blockIdx.x; u < p.units; u += G, ++j) {
             const int a = j & 1, nbi = u / p.kspl, ks = u % p.kspl, n0 = nbi * p.nblk, nb = min(p.nblk, p.N - n0);
-            if (et < kGemmMaxB) {
-                bs->rmax[et] = 0u;
-                bs->best[et] = 0ull;
-            }
+            if (et < kGemmMaxB) bs->best[et] = 0ull;
             bool got = mbar_wait_bounded(&bs->dfull[a], (j >> 1) & 1, p.err, globaltimer_ns() + p.timeout_ns,
                                          kDevTimeoutFull);
             if (bar_red_or(kBarEpi, 128, !got)) break;  // uniform exit
@@ -321,56 +325,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 }
             }
             named_bar_sync(kBarEpi, 128);
-            if (et < p.B) {
-                if (p.op == kGemmSwiGLU && bs->rmax[et]) atomicMax(p.hmax + et, bs->rmax[et]);
-                if (p.op == kGemmLogits && bs->best[et]) atomicMax(p.best + et, bs->best[et]);
-            }
+            if (et < p.B && p.op == kGemmLogits && bs->best[et]) atomicMax(p.best + et, bs->best[et]);
             named_bar_sync(kBarEpi, 128);
-        }
-    } else {
-        // ---------------------------------------------------------- A loader --
-        const int lt = threadIdx.x - kLoadT0;
-        const int items = ((p.B + 3) >> 2) * 64;  // (4 sequences x 8 octets x hi / lo) blocks
-        uint32_t it = 0;
-        bool ok = true;
-        for (int u = blockIdx.x; u < p.units && ok; u += G) {
-            const int ks = u % p.kspl;
-            for (int c = 0; c < nchunk; ++c, ++it) {
-                const uint32_t slot = it % kStages, par = ((it / kStages) & 1u) ^ 1u;
-                if (!wait_warp(&bs->empty[slot], par, p, kDevTimeoutEmpty)) {
-                    ok = false;
-                    break;
-                }
-                const int kc = ks * krange + c * kKC;
-                uint8_t* ab = smem + slot * kStageBytes;
-                for (int i = lt; i < items; i += 128) {
-                    // 8 consecutive items = rows 0..7 of one core matrix (128 B)
-                    const int part = i & 1, sl = (i >> 1) & 3, o = (i >> 3) & 7, s4 = i >> 6, s = 4 * s4 + sl;
-                    if (s < p.B) {
-                        const float4* src = reinterpret_cast<const float4*>(p.A + (size_t)s * p.lda + kc + 8 * o);
-                        const float4 x0 = __ldcg(src), x1 = __ldcg(src + 1);
-                        const float sc = __int_as_float((127 + row_exp(__ldg(p.rowmax + s))) << 23);
-                        const float f[8] = {x0.x * sc, x0.y * sc, x0.z * sc, x0.w * sc,
-                                            x1.x * sc, x1.y * sc, x1.z * sc, x1.w * sc};
-                        uint32_t w[4];
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            const __half2 hh = __floats2half2_rn(f[2 * k], f[2 * k + 1]);
-                            if (part == 0) {
-                                w[k] = *reinterpret_cast<const uint32_t*>(&hh);
-                            } else {
-                                const float2 hf = __half22float2(hh);
-                                w[k] = pack_h2(f[2 * k] - hf.x, f[2 * k + 1] - hf.y);
-                            }
-                        }
-                        *reinterpret_cast<uint4*>(ab + s4 * 1024 + o * 128 + (2 * sl + part) * 16) =
-                            make_uint4(w[0], w[1], w[2], w[3]);
-                    }
-                }
-                fence_async_shared();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bs->afull[slot]);
-            }
         }
     }
 
@@ -380,17 +336,44 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
-__global__ void rowmax_kernel(const float* __restrict__ A, int lda, int K, float* __restrict__ out) {
-    const float* a = A + (size_t)blockIdx.x * lda;
+// One activation row per CTA: max |A[s][k]|, the row scale 2^e with
+// max * 2^e in [2^14, 2^15), then hi = f16(a * 2^e), lo = f16(a * 2^e - hi)
+// into the pre-split layout (MMA rows 2 (s % 4) and 2 (s % 4) + 1 of row
+// group s / 4).
+__global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ A, int lda, int K,
+                                                         uint8_t* __restrict__ As, float* __restrict__ unscale) {
+    const int s = blockIdx.x;
+    const float* a = A + (size_t)s * lda;
     float m = 0.0f;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) m = fmaxf(m, fabsf(a[k]));
+    for (int k = threadIdx.x * 4; k < K; k += 256 * 4) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(a + k));
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
     m = warp_max(m);
     __shared__ float red[8];
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
-        out[blockIdx.x] = m;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) m = fmaxf(m, red[w]);
+    const int e = row_exp(m);
+    const float sc = __int_as_float((127 + e) << 23);
+    if (threadIdx.x == 0) unscale[s] = __int_as_float((127 - e) << 23);
+    uint8_t* base = As + (size_t)(s >> 2) * (size_t)(K >> 3) * 128 + (2 * (s & 3)) * 16;
+    for (int o = threadIdx.x; o < (K >> 3); o += 256) {
+        const float4 x0 = __ldcg(reinterpret_cast<const float4*>(a + 8 * o));
+        const float4 x1 = __ldcg(reinterpret_cast<const float4*>(a + 8 * o + 4));
+        const float f[8] = {x0.x * sc, x0.y * sc, x0.z * sc, x0.w * sc, x1.x * sc, x1.y * sc, x1.z * sc, x1.w * sc};
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const __half2 hh = __floats2half2_rn(f[2 * k], f[2 * k + 1]);
+            const float2 hf = __half22float2(hh);
+            hi[k] = *reinterpret_cast<const uint32_t*>(&hh);
+            lo[k] = pack_h2(f[2 * k] - hf.x, f[2 * k + 1] - hf.y);
+        }
+        uint4* d = reinterpret_cast<uint4*>(base + (size_t)o * 128);
+        d[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        d[1] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
 }
 
@@ -398,25 +381,33 @@ __global__ void rowmax_kernel(const float* __restrict__ A, int lda, int K, float
 
 bool gemm_plan(GemmParams* p, int num_sms) {
     if (p->B < 1 || p->B > kGemmMaxB || p->N < 16 || p->N % 16 || p->K < kKC || p->K % kKC || p->cbw < kKC ||
-        p->cbw % kKC || p->K % p->cbw || p->lda % 4)
+        p->cbw % kKC || p->K % p->cbw)
         return false;
-    const int G = num_sms > 0 ? num_sms : 1;
+    const int G = num_sms > 0 ? num_sms : 1, nrg = (p->B + 3) / 4;
     double best = 1e300;
     for (int nblk = kMaxN; nblk >= 16; nblk -= 16) {
         const int nbk = (p->N + nblk - 1) / nblk;
+        const int sb = kABytes + nblk * kKC * 2;
+        int stages = kRingBytes / sb;
+        if (stages > kMaxStages) stages = kMaxStages;
+        // Weight bytes in flight per SM; below ~96 KB the stream is latency-bound.
+        const double inflight = (double)stages * nblk * kKC * 2;
+        const double bw = inflight < 96.0 * 1024 ? inflight / (96.0 * 1024) : 1.0;
         for (int kspl = 1; kspl <= 32; kspl *= 2) {
             if (p->K % (kspl * kKC)) continue;
             const int krange = p->K / kspl, units = nbk * kspl, waves = (units + G - 1) / G;
-            // Per-CTA time of the slowest wave in bytes: weights (HBM), A (L2,
-            // cheaper), a fixed cost per unit (pipeline fill, epilogue) and
-            // the partial round trip of split units.
-            double cost = waves * ((double)nblk * krange * 2 + 0.35 * p->B * krange * 4 + 64 * 1024);
-            if (kspl > 1) cost += 0.5 * (double)kspl * p->B * nblk * 4 + 32 * 1024;
+            // Per-CTA time of the slowest wave in bytes: weights (HBM), the
+            // pre-split activations (L2, cheaper), a fixed cost per unit
+            // (pipeline fill, epilogue) and the partial round trip of splits.
+            double cost = waves * (((double)nblk * krange * 2 + 0.35 * nrg * krange * 16) / bw + 48 * 1024);
+            if (kspl > 1) cost += 0.5 * (double)kspl * p->B * nblk * 4 + 24 * 1024;
             if (cost < best * 0.999) {
                 best = cost;
                 p->nblk = nblk;
                 p->kspl = kspl;
                 p->units = units;
+                p->stages = stages;
+                p->stage_bytes = sb;
             }
         }
     }
@@ -436,17 +427,65 @@ int gemm_tile_width(int cols) {
 }
 
 cudaError_t gemm_prepare() {
-    return cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    return cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemMax);
 }
 
-cudaError_t launch_gemm(const GemmParams& p, int num_sms, cudaStream_t st) {
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }
+    return fn;
+}
+}  // namespace
+
+cudaError_t gemm_make_wmap(CUtensorMap* out, const GemmParams& p) {
+    auto enc = encode_fn();
+    if (!enc || ((uintptr_t)p.W & 15)) return cudaErrorInvalidValue;
+    // Element (i, o, cb, g) = half i of octet o of tile (g, cb): the tiled layout.
+    const int ncb = p.K / p.cbw;
+    cuuint64_t dims[4] = {64, (cuuint64_t)(p.cbw / 8), (cuuint64_t)ncb, (cuuint64_t)(p.N / 8)};
+    cuuint64_t strides[3] = {128, (cuuint64_t)p.cbw * 16, (cuuint64_t)ncb * p.cbw * 16};
+    cuuint32_t box[4] = {64, kKC / 8, 1, (cuuint32_t)(p.nblk / 8)};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<__half*>(p.W), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t gemm_make_amap(CUtensorMap* out, const GemmParams& p) {
+    auto enc = encode_fn();
+    if (!enc || ((uintptr_t)p.As & 15)) return cudaErrorInvalidValue;
+    const int nrg = (p.B + 3) / 4;
+    cuuint64_t dims[3] = {64, (cuuint64_t)(p.K / 8), (cuuint64_t)nrg};
+    cuuint64_t strides[2] = {128, (cuuint64_t)(p.K / 8) * 128};
+    cuuint32_t box[3] = {64, kKC / 8, (cuuint32_t)nrg};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint8_t*>(p.As), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemm(const GemmParams& p, const CUtensorMap& wmap, const CUtensorMap& amap, int num_sms,
+                        cudaStream_t st) {
+    if (p.stages < 2 || p.stages > kMaxStages || p.stages * p.stage_bytes > kRingBytes || p.nblk % 16 ||
+        p.nblk > kMaxN || p.units < 1)
+        return cudaErrorInvalidValue;
     const int grid = p.units < num_sms ? p.units : num_sms;
-    gemm_kernel<<<grid, kThreads, kSmemBytes, st>>>(p);
+    const int smem = p.stages * p.stage_bytes + (int)sizeof(Bars);
+    gemm_kernel<<<grid, kThreads, smem, st>>>(p, wmap, amap);
     return cudaGetLastError();
 }
 
-cudaError_t launch_rowmax(const float* A, int lda, int K, int B, float* rowmax, cudaStream_t st) {
-    rowmax_kernel<<<B, 256, 0, st>>>(A, lda, K, rowmax);
+cudaError_t launch_gemm_split(const float* A, int lda, int K, int B, uint8_t* As, float* unscale, cudaStream_t st) {
+    split_rows_kernel<<<B, 256, 0, st>>>(A, lda, K, As, unscale);
     return cudaGetLastError();
 }
 

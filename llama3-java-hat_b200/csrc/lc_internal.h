@@ -1,6 +1,7 @@
 // lc_internal.h -- declarations shared by the llamacuda translation units.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -170,27 +171,34 @@ cudaError_t launch_decode_traced(const DecodeParams& p, const DecodeLaunch& l, c
 // ---- batched GEMM on tcgen05 (lc_gemm.cu) ----
 //
 // Y[s][n] = sum_k A[s][k] * W[n][k] for B <= 64 activation rows, W F16 in the
-// tiled layout above (column-block width cbw), A fp32 with rowmax[s] =
-// max_k |A[s][k]| supplied (the power-of-two scale of the hi / lo split).
-// The result goes through one of the fused epilogues.
+// tiled layout above (column-block width cbw).  A reaches the GEMM pre-split
+// (launch_gemm_split or a fused producer): row s becomes f16 hi / lo parts
+// under a power-of-two row scale, MMA rows 2s (hi) and 2s + 1 (lo), stored as
+// [16 row groups of 8 MMA rows][K / 8 octets][8 rows][8 halves] (bytes
+// ((s / 4) * (K / 8) + k / 8) * 128 + (2 * (s % 4) + part) * 16 + (k % 8) * 2),
+// and unscale[s] = 2^-e.  The result goes through one of the fused epilogues.
 enum GemmOp : int {
     kGemmStore = 0,   // y[s * ldy + n] = v
     kGemmResid = 1,   // y[s * ldy + n] += v (residual add, in place)
     kGemmQKV = 2,     // RoPE on q and k, q -> q[s][n], k / v -> the KV cache at pos[s]
-    kGemmSwiGLU = 3,  // rows 4m..4m+3 = (gate, up) pairs: h[s][2m + j] = silu(g) * u; hmax[s] = max |h|
+    kGemmSwiGLU = 3,  // rows 4m..4m+3 = (gate, up) pairs: h[s][2m + j] = silu(g) * u
     kGemmLogits = 4,  // logits[s][n] (optional) and best[s] = packed (value, lowest index) argmax
 };
 
 constexpr int kGemmMaxB = 64;
 constexpr int kGemmHeadDim = 64;  // head_dim of the kGemmQKV epilogue
 
+// Bytes of the pre-split activations of B rows and K columns.
+inline size_t gemm_split_bytes(int B, int K) { return (size_t)((B + 3) / 4) * (size_t)K * 16; }
+
 struct GemmParams {
     const __half* W;  // tiled
     int N, K, cbw;    // rows, columns, column-block width (K % cbw == 0, cbw % 64 == 0)
-    const float* A;   // [B][lda]
-    int lda, B;
-    const float* rowmax;  // [B]
-    int nblk, kspl, units;   // N-block rows, K splits, (N-blocks) * kspl
+    const uint8_t* As;      // pre-split activations
+    const float* unscale;   // [B]
+    int B;
+    int nblk, kspl, units;  // N-block rows, K splits, (N-blocks) * kspl
+    int stages, stage_bytes;
     float* part;             // [kspl][B][N] partial sums when kspl > 1
     uint32_t* tickets;       // [N-blocks], zero between launches, when kspl > 1
     int op;
@@ -207,7 +215,6 @@ struct GemmParams {
     // kGemmSwiGLU
     float* h;
     int ldh;
-    uint32_t* hmax;           // [B] float bits of max |h|, atomicMax
     // kGemmLogits
     float* logits;
     int ldl;
@@ -216,16 +223,22 @@ struct GemmParams {
     uint64_t timeout_ns;
 };
 
-// Chooses nblk and kspl for a grid of `num_sms` CTAs; fills units.  Returns
-// false when the shape is unsupported (N % 16, K % 64, K % cbw, B range).
+// Chooses nblk, kspl and the ring for a grid of `num_sms` CTAs; fills units.
+// Returns false when the shape is unsupported (N % 16, K % 64, K % cbw, B range).
 bool gemm_plan(GemmParams* p, int num_sms);
 // Bytes of the partial-sum buffer p needs (0 when kspl == 1).
 size_t gemm_part_bytes(const GemmParams& p);
 cudaError_t gemm_prepare();  // sets the shared-memory attribute once
-cudaError_t launch_gemm(const GemmParams& p, int num_sms, cudaStream_t st);
-// rowmax[s] = max |A[s][0..K)| (float bits) for the standalone entry point.
-cudaError_t launch_rowmax(const float* A, int lda, int K, int B, float* rowmax, cudaStream_t st);
-// Row-major F16 [rows][cols] -> tiled layout with column-block width cbw.
+// TMA tensor maps: the tiled weights of p (box: nblk rows x 64 columns) and
+// the pre-split activations of p.B rows (box: all row groups x 64 columns).
+cudaError_t gemm_make_wmap(CUtensorMap* out, const GemmParams& p);
+cudaError_t gemm_make_amap(CUtensorMap* out, const GemmParams& p);
+cudaError_t launch_gemm(const GemmParams& p, const CUtensorMap& wmap, const CUtensorMap& amap, int num_sms,
+                        cudaStream_t st);
+// A fp32 [B][lda] -> pre-split activations As and unscale[B].
+cudaError_t launch_gemm_split(const float* A, int lda, int K, int B, uint8_t* As, float* unscale, cudaStream_t st);
+// Column-block width of the standalone tiled layout: the largest multiple of
+// 64 up to 2048 dividing cols (0: cols % 64 != 0).
 int gemm_tile_width(int cols);
 
 // Argmax key: order-preserving float bits above the inverted index, so the

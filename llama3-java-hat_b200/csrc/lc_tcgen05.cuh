@@ -32,6 +32,28 @@ __host__ __device__ constexpr uint32_t tc_idesc_f16_f32(int M, int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Tiled TMA loads (cp.async.bulk.tensor, no multicast) of one box into this
+// CTA's shared memory, completion as transaction bytes on `bar`.  `tmap` is
+// the generic address of a __grid_constant__ CUtensorMap; the innermost
+// coordinate c0 is 0 at every call site (the box spans the whole 128-byte
+// inner dimension), so it is always 16-byte aligned.
+LC_DEV void tma_load_4d(void* dst, const void* tmap, int c0, int c1, int c2, int c3, uint64_t* bar,
+                        uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+LC_DEV void tma_load_3d(void* dst, const void* tmap, int c0, int c1, int c2, uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
 // TMEM allocation by one full warp: the base address is written to *slot.
 // ncols is a power of two >= 32.
 LC_DEV void tmem_alloc(uint32_t* slot, uint32_t ncols) {

@@ -256,6 +256,36 @@ int lc_session_read_trace(lc_session* s, uint64_t* out, int64_t n_words, int32_t
  * (CUDA events on the session stream). */
 int lc_session_last_ms(lc_session* s, float* ms);
 
+/* ------------------------------------------------- multi-sequence batch ---
+ * Greedy decode of up to 64 independent sequences in lockstep (serving).  No
+ * reference counterpart: the reference serves one sequence per
+ * LlamaInference (H/LlamaInference.java:173-217); each sequence of a batch
+ * gets exactly that computation, with every weight matrix read once per
+ * step for all sequences (tcgen05 tensor-core products).  A batch owns KV
+ * caches for max_batch sequences of the model's max_seq positions. */
+typedef struct lc_batch lc_batch;
+
+int lc_batch_create(lc_model* m, int32_t max_batch, lc_batch** out);
+int lc_batch_destroy(lc_batch* b);
+
+/* LlamaInference.generate(prompt_s, max_new, stop) (H/LlamaInference.java
+ * :180-217) for n_seqs sequences at once.  prompts: the prompts concatenated
+ * (host), prompt_lens[n_seqs] >= 1; prompt_lens[s] + max_new - 1 <= max_seq.
+ * out_tokens [n_seqs][max_new] (host) receives each sequence's generated
+ * tokens, the stop token included; entries after a stop token are -1.
+ * Synchronous. */
+int lc_batch_generate(lc_batch* b, int32_t n_seqs, const int32_t* prompts, const int32_t* prompt_lens,
+                      int32_t max_new, const int32_t* stop, int32_t n_stop, int32_t* out_tokens);
+
+/* Device time of the last lc_batch_generate in ms: all steps, and the steps
+ * from the last prompt position on (each of which yields one token per
+ * sequence); steps = positions run. */
+int lc_batch_last_ms(lc_batch* b, float* total_ms, float* decode_ms, int32_t* steps);
+
+/* Logits (vocab floats, host) of sequence `seq` at the last position of the
+ * last lc_batch_generate. */
+int lc_batch_logits(lc_batch* b, int32_t seq, float* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -361,6 +361,7 @@ extern "C" int lc_gemm_f16_tiled(lc_context* c, const uint16_t* Wt, const float*
     g.op = kGemmStore;
     g.y = dY;
     g.ldy = rows;
+    g.n_valid = rows;
     g.err = c->d_err;
     g.timeout_ns = 2000000000ull;
     CUtensorMap wmap, amap;
@@ -1143,6 +1144,107 @@ extern "C" int lc_session_read_trace(lc_session* s, uint64_t* out, int64_t n_wor
 extern "C" int lc_session_last_ms(lc_session* s, float* ms) {
     if (!s || !ms) return fail(LC_ERR_INVALID_ARG, "NULL argument");
     *ms = s->last_ms;
+    return LC_OK;
+}
+
+// ------------------------------------------------------------ batch ----
+
+struct lc_batch {
+    lc_model* m = nullptr;
+    BatchEngine* e = nullptr;
+};
+
+extern "C" int lc_batch_create(lc_model* m, int32_t max_batch, lc_batch** out) {
+    if (!m || !out) return fail(LC_ERR_INVALID_ARG, "NULL argument");
+    CTX_CHECK(m->ctx);
+    if (!m->finalized) return fail(LC_ERR_STATE, "model not finalized");
+    if (max_batch < 1 || max_batch > kGemmMaxB) return fail(LC_ERR_INVALID_ARG, "max_batch %d not in 1..%d", max_batch, kGemmMaxB);
+    BatchModel bm;
+    const lc_config& c = m->cfg;
+    bm.dim = c.dim;
+    bm.hidden = c.hidden;
+    bm.n_layers = c.n_layers;
+    bm.n_heads = c.n_heads;
+    bm.n_kv = c.n_kv_heads;
+    bm.head_dim = c.head_dim;
+    bm.vocab = c.vocab;
+    bm.max_seq = c.max_seq;
+    bm.eps = c.rms_eps;
+    bm.tok_emb = m->tok_emb;
+    bm.lm_head = m->lm_tiled;
+    bm.out_norm = m->out_norm;
+    for (const LayerStore& L : m->layers) bm.layers.push_back({L.wqkv, L.wo, L.wgu, L.wdown, L.attn_norm, L.ffn_norm});
+    bm.rope = m->rope;
+    const char* why = nullptr;
+    if (!batch_supported(bm, &why)) return fail(LC_ERR_UNSUPPORTED, "%s", why);
+    cudaError_t ce;
+    BatchEngine* e = batch_create(bm, max_batch, m->ctx->sms, m->ctx->stream, m->ctx->d_err, &ce);
+    if (!e) return cuda_fail(ce, "batch buffers");
+    lc_batch* b = new lc_batch();
+    b->m = m;
+    b->e = e;
+    *out = b;
+    return LC_OK;
+}
+
+extern "C" int lc_batch_destroy(lc_batch* b) {
+    if (!b) return LC_OK;
+    cudaSetDevice(b->m->ctx->device);
+    batch_destroy(b->e);
+    delete b;
+    return LC_OK;
+}
+
+extern "C" int lc_batch_generate(lc_batch* b, int32_t n, const int32_t* prompts, const int32_t* lens,
+                                 int32_t max_new, const int32_t* stop, int32_t n_stop, int32_t* out) {
+    if (!b || !prompts || !lens || !out) return fail(LC_ERR_INVALID_ARG, "NULL argument");
+    CTX_CHECK(b->m->ctx);
+    const lc_config& c = b->m->cfg;
+    if (n < 1 || n > batch_max(b->e)) return fail(LC_ERR_INVALID_ARG, "n_seqs %d not in 1..%d", n, batch_max(b->e));
+    if (max_new < 1) return fail(LC_ERR_INVALID_ARG, "max_new %d", max_new);
+    if (n_stop < 0 || n_stop > kMaxStop || (n_stop > 0 && !stop)) return fail(LC_ERR_INVALID_ARG, "n_stop %d", n_stop);
+    const int ts = batch_tok_stride(b->e);
+    std::vector<int32_t> tok((size_t)n * ts, 0), L(lens, lens + n);
+    size_t off = 0;
+    for (int s = 0; s < n; ++s) {
+        if (L[s] < 1 || L[s] + max_new - 1 > c.max_seq)
+            return fail(LC_ERR_INVALID_ARG, "sequence %d: prompt length %d + max_new %d exceeds max_seq %d", s, L[s], max_new, c.max_seq);
+        for (int i = 0; i < L[s]; ++i) {
+            const int32_t t = prompts[off + i];
+            if (t < 0 || t >= c.vocab) return fail(LC_ERR_INVALID_ARG, "sequence %d: token %d out of range", s, t);
+            tok[(size_t)s * ts + i] = t;
+        }
+        off += L[s];
+    }
+    std::vector<int32_t> res;
+    cudaError_t ce = batch_run(b->e, n, tok, L, max_new, &res);
+    if (ce != cudaSuccess) return cuda_fail(ce, "batch generate");
+    int rc = check_device_error(b->m->ctx);
+    if (rc) return rc;
+    for (int s = 0; s < n; ++s) {
+        bool stopped = false;
+        for (int i = 0; i < max_new; ++i) {
+            int32_t t = stopped ? -1 : res[(size_t)s * ts + L[s] + i];
+            out[(size_t)s * max_new + i] = t;
+            for (int k = 0; k < n_stop && !stopped; ++k) stopped = (t == stop[k]);
+        }
+    }
+    return LC_OK;
+}
+
+extern "C" int lc_batch_last_ms(lc_batch* b, float* total_ms, float* decode_ms, int32_t* steps) {
+    if (!b || !total_ms || !decode_ms) return fail(LC_ERR_INVALID_ARG, "NULL argument");
+    int st = 0;
+    batch_times(b->e, total_ms, decode_ms, &st);
+    if (steps) *steps = st;
+    return LC_OK;
+}
+
+extern "C" int lc_batch_logits(lc_batch* b, int32_t seq, float* out) {
+    if (!b || !out) return fail(LC_ERR_INVALID_ARG, "NULL argument");
+    CTX_CHECK(b->m->ctx);
+    if (seq < 0 || seq >= batch_max(b->e)) return fail(LC_ERR_INVALID_ARG, "seq %d", seq);
+    CK(batch_logits(b->e, seq, out), "read logits");
     return LC_OK;
 }
 

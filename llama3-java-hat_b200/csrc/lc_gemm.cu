@@ -63,18 +63,6 @@ struct Bars {
 };
 constexpr int kSmemMax = kRingBytes + (int)sizeof(Bars);
 
-// Row scale of the hi / lo split (same rule as the fused decode kernel).
-__device__ __forceinline__ int row_exp(float m) {
-    if (!(m > 0.0f)) return 0;
-    int e = 14 - (((__float_as_int(m) >> 23) & 0xff) - 127);
-    return e < -126 ? -126 : (e > 126 ? 126 : e);
-}
-
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t*>(&h);
-}
-
 // RoPE of one interleaved pair (RoPE.java:42-49): angle pos * freq in float,
 // cos / sin in double rounded to float, products and sums not contracted.
 __device__ __forceinline__ void rope2(float& v0, float& v1, int pos, float freq) {
@@ -136,6 +124,7 @@ __device__ __forceinline__ void apply4(const GemmParams& p, Bars* bs, int s, int
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 unsigned long long kj = 0;
+                if (n + j >= p.n_valid) break;
                 if (y[j] == y[j]) kj = argmax_key(y[j], n + j);
                 else if (n + j == 0) kj = ~0ull;  // NaN at index 0: LlamaInference.argmax returns 0
                 k = kj > k ? kj : k;
@@ -146,13 +135,6 @@ __device__ __forceinline__ void apply4(const GemmParams& p, Bars* bs, int s, int
     }
 }
 
-__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t par, const GemmParams& p, int code) {
-    int ok = 1;
-    if ((threadIdx.x & 31) == 0)
-        ok = mbar_wait_bounded(bar, par, p.err, globaltimer_ns() + p.timeout_ns, code) ? 1 : 0;
-    return __shfl_sync(0xffffffffu, ok, 0) != 0;
-}
-
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ GemmParams p,
                                                            const __grid_constant__ CUtensorMap wmap,
                                                            const __grid_constant__ CUtensorMap amap) {
@@ -160,7 +142,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const int NS = p.stages, SB = p.stage_bytes;
     Bars* bs = reinterpret_cast<Bars*>(smem + NS * SB);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = gridDim.x;
-    const int krange = p.K / p.kspl, nchunk = krange / kKC, ncb = p.K / p.cbw, nrg = (p.B + 3) >> 2;
+    const int krange = p.K / p.kspl, nchunk = krange / kKC, nrg = (p.B + 3) >> 2;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -355,25 +337,15 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
     __syncthreads();
 #pragma unroll
     for (int w = 0; w < 8; ++w) m = fmaxf(m, red[w]);
-    const int e = row_exp(m);
-    const float sc = __int_as_float((127 + e) << 23);
-    if (threadIdx.x == 0) unscale[s] = __int_as_float((127 - e) << 23);
-    uint8_t* base = As + (size_t)(s >> 2) * (size_t)(K >> 3) * 128 + (2 * (s & 3)) * 16;
+    const int e = split_row_exp(m);
+    const float sc = pow2f(e);
+    if (threadIdx.x == 0) unscale[s] = pow2f(-e);
     for (int o = threadIdx.x; o < (K >> 3); o += 256) {
         const float4 x0 = __ldcg(reinterpret_cast<const float4*>(a + 8 * o));
         const float4 x1 = __ldcg(reinterpret_cast<const float4*>(a + 8 * o + 4));
         const float f[8] = {x0.x * sc, x0.y * sc, x0.z * sc, x0.w * sc, x1.x * sc, x1.y * sc, x1.z * sc, x1.w * sc};
-        uint32_t hi[4], lo[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const __half2 hh = __floats2half2_rn(f[2 * k], f[2 * k + 1]);
-            const float2 hf = __half22float2(hh);
-            hi[k] = *reinterpret_cast<const uint32_t*>(&hh);
-            lo[k] = pack_h2(f[2 * k] - hf.x, f[2 * k + 1] - hf.y);
-        }
-        uint4* d = reinterpret_cast<uint4*>(base + (size_t)o * 128);
-        d[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        d[1] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        uint4* d = reinterpret_cast<uint4*>(As + split_offset(s, o, K));
+        split_octet(f, d[0], d[1]);
     }
 }
 
@@ -449,7 +421,8 @@ cudaError_t gemm_make_wmap(CUtensorMap* out, const GemmParams& p) {
     if (!enc || ((uintptr_t)p.W & 15)) return cudaErrorInvalidValue;
     // Element (i, o, cb, g) = half i of octet o of tile (g, cb): the tiled layout.
     const int ncb = p.K / p.cbw;
-    cuuint64_t dims[4] = {64, (cuuint64_t)(p.cbw / 8), (cuuint64_t)ncb, (cuuint64_t)(p.N / 8)};
+    const int rows = p.rows_mem > 0 ? p.rows_mem : p.N;  // rows stored; the rest of the last box reads zeros
+    cuuint64_t dims[4] = {64, (cuuint64_t)(p.cbw / 8), (cuuint64_t)ncb, (cuuint64_t)(rows / 8)};
     cuuint64_t strides[3] = {128, (cuuint64_t)p.cbw * 16, (cuuint64_t)ncb * p.cbw * 16};
     cuuint32_t box[4] = {64, kKC / 8, 1, (cuuint32_t)(p.nblk / 8)};
     cuuint32_t es[4] = {1, 1, 1, 1};

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -194,6 +195,7 @@ inline size_t gemm_split_bytes(int B, int K) { return (size_t)((B + 3) / 4) * (s
 struct GemmParams {
     const __half* W;  // tiled
     int N, K, cbw;    // rows, columns, column-block width (K % cbw == 0, cbw % 64 == 0)
+    int rows_mem;     // rows stored in W (multiple of 8, <= N; 0: N)
     const uint8_t* As;      // pre-split activations
     const float* unscale;   // [B]
     int B;
@@ -218,6 +220,7 @@ struct GemmParams {
     // kGemmLogits
     float* logits;
     int ldl;
+    int n_valid;              // columns >= n_valid are padding (kGemmLogits)
     unsigned long long* best; // [B]
     int* err;
     uint64_t timeout_ns;
@@ -240,6 +243,33 @@ cudaError_t launch_gemm_split(const float* A, int lda, int K, int B, uint8_t* As
 // Column-block width of the standalone tiled layout: the largest multiple of
 // 64 up to 2048 dividing cols (0: cols % 64 != 0).
 int gemm_tile_width(int cols);
+
+// ---- multi-sequence greedy decode (lc_batch.cu) ----
+struct BatchModel {
+    int dim, hidden, n_layers, n_heads, n_kv, head_dim, vocab, max_seq;
+    float eps;
+    const __half* tok_emb;   // row-major [vocab][dim]
+    const __half* lm_head;   // tiled, rows padded to a multiple of 8
+    const float* out_norm;
+    std::vector<LayerW> layers;  // host copy of the layer table (device pointers)
+    RopeFreq rope;
+};
+struct BatchEngine;
+bool batch_supported(const BatchModel& m, const char** why);
+// Buffers for up to max_batch (1..64) sequences of up to m.max_seq positions.
+BatchEngine* batch_create(const BatchModel& m, int max_batch, int num_sms, cudaStream_t st, int* err,
+                          cudaError_t* ce);
+void batch_destroy(BatchEngine* e);
+int batch_max(const BatchEngine* e);
+int batch_tok_stride(const BatchEngine* e);  // max_seq + 1
+// Greedy generation of n sequences: tok_host [n][tok_stride] holds the
+// prompts, lens their lengths (validated by the caller: tokens in range,
+// lens[s] + max_new - 1 <= max_seq).  tok_out receives the token rows:
+// prompt, then the generated tokens.
+cudaError_t batch_run(BatchEngine* e, int n, const std::vector<int32_t>& tok_host, const std::vector<int32_t>& lens,
+                      int max_new, std::vector<int32_t>* tok_out);
+void batch_times(const BatchEngine* e, float* total_ms, float* decode_ms, int* steps);
+cudaError_t batch_logits(const BatchEngine* e, int s, float* out);  // logits of the last lm_head step
 
 // Argmax key: order-preserving float bits above the inverted index, so the
 // largest key is the largest value with the lowest index.

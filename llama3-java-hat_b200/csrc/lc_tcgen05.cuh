@@ -8,8 +8,9 @@
 // matrices of one operand tile sit 128 B apart along K (leading byte offset)
 // and 1024 B apart along M / N (stride byte offset), i.e. a tile of R rows x
 // 64 columns is [R/8 row groups][8 column octets][8 rows][8 halves].  This is
-// exactly the order of the tiled weight layout (lc_internal.h), so weight
-// tiles reach shared memory with plain 1-D bulk copies.
+// the order of the tiled weight layout (lc_internal.h) and of the pre-split
+// activations, so a TMA box of either lands in shared memory ready for the
+// MMA, without a swizzle.
 #pragma once
 
 #include "lc_common.cuh"
@@ -111,6 +112,41 @@ LC_DEV void tmem_wait_ld(uint32_t (&v)[16]) {
                    "+r"(v[15])
                  :
                  : "memory");
+}
+
+// ---------------------------------------------- hi / lo split of operand A --
+//
+// An fp32 activation row becomes two f16 rows under a power-of-two row scale
+// 2^e chosen so that max |a| * 2^e lies in [2^14, 2^15): hi = f16(a * 2^e),
+// lo = f16(a * 2^e - hi).  The subtraction is exact (hi is a * 2^e rounded to
+// 11 bits), hi + lo = a * 2^e to 2^-22 relative, and both stay in f16 range.
+LC_DEV int split_row_exp(float m) {
+    if (!(m > 0.0f)) return 0;
+    int e = 14 - (((__float_as_int(m) >> 23) & 0xff) - 127);
+    return e < -126 ? -126 : (e > 126 ? 126 : e);
+}
+
+LC_DEV float pow2f(int e) { return __int_as_float((127 + e) << 23); }
+
+// Eight scaled values -> the hi and lo 16-byte rows of one core matrix.
+LC_DEV void split_octet(const float (&f)[8], uint4& hi, uint4& lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const __half2 hh = __floats2half2_rn(f[2 * k], f[2 * k + 1]);
+        const float2 hf = __half22float2(hh);
+        const __half2 ll = __floats2half2_rn(f[2 * k] - hf.x, f[2 * k + 1] - hf.y);
+        h[k] = *reinterpret_cast<const uint32_t*>(&hh);
+        l[k] = *reinterpret_cast<const uint32_t*>(&ll);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Byte offset of octet o of activation row s in the pre-split layout with K
+// columns: row group s / 4, MMA row 2 (s % 4) (hi; +16 bytes: lo).
+__host__ __device__ inline size_t split_offset(int s, int o, int K) {
+    return ((size_t)(s >> 2) * (size_t)(K >> 3) + (size_t)o) * 128 + (size_t)(2 * (s & 3)) * 16;
 }
 
 }  // namespace lc

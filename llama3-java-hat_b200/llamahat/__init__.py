@@ -9,10 +9,10 @@ from .config import LLAMA_3_2_1B, TINY, LlamaConfig
 from .kernels import (Accelerator, CudaAttention, CudaGEMV, CudaKernelFactory, CudaRMSNorm, CudaRoPE, CudaSiLU,
                       CudaSoftmax, IAttention, IGEMV, IKernelFactory, IRMSNorm, IRoPE, ISiLU, ISoftmax,
                       default_accelerator)
-from .inference import EOS_TOKEN, CudaModel, LlamaInference, Session
+from .inference import EOS_TOKEN, Batch, CudaModel, LlamaInference, Session
 
 __all__ = [
-    "Accelerator", "CudaAttention", "CudaGEMV", "CudaKernelFactory", "CudaModel", "CudaRMSNorm", "CudaRoPE",
+    "Accelerator", "Batch", "CudaAttention", "CudaGEMV", "CudaKernelFactory", "CudaModel", "CudaRMSNorm", "CudaRoPE",
     "CudaSiLU", "CudaSoftmax", "DeviceTimeoutError", "EOS_TOKEN", "IAttention", "IGEMV", "IKernelFactory",
     "IRMSNorm", "IRoPE", "ISiLU", "ISoftmax", "IllegalArgumentError", "IllegalStateError", "LLAMA_3_2_1B",
     "LlamaConfig", "LlamaCudaError", "LlamaInference", "ModelIOError", "Session", "TINY", "default_accelerator",

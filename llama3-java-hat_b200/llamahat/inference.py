@@ -120,6 +120,52 @@ class Session:
         self._fin()
 
 
+class Batch:
+    """Up to 64 independent sequences decoded in lockstep (serving): each
+    sequence gets LlamaInference.generate's computation, every weight matrix
+    is read once per step for all of them."""
+
+    def __init__(self, model: CudaModel, max_batch: int):
+        self.model = model
+        lib = _lib.load()
+        h = ctypes.c_void_p()
+        _lib.check(lib.lc_batch_create(model.handle, int(max_batch), ctypes.byref(h)))
+        self.handle = h
+        self.max_batch = int(max_batch)
+        self._fin = weakref.finalize(self, lib.lc_batch_destroy, h)
+
+    def generate(self, prompts, max_new: int, stop=(EOS_TOKEN,)) -> list[np.ndarray]:
+        """Greedy tokens per sequence (stop token included, as generate)."""
+        lib = _lib.load()
+        ps = [np.asarray(p, dtype=np.int32).ravel() for p in prompts]
+        lens = np.array([p.size for p in ps], np.int32)
+        flat = np.ascontiguousarray(np.concatenate(ps) if ps else np.zeros(0, np.int32))
+        st = np.ascontiguousarray(np.asarray(sorted(stop) if stop else [], dtype=np.int32))
+        out = np.zeros((len(ps), max(int(max_new), 1)), np.int32)
+        _lib.check(lib.lc_batch_generate(self.handle, len(ps), flat.ctypes.data, lens.ctypes.data, int(max_new),
+                                         st.ctypes.data if st.size else None, st.size, out.ctypes.data))
+        res = []
+        for row in out:
+            k = int(np.argmax(row < 0)) if (row < 0).any() else row.size
+            res.append(row[:k].copy())
+        return res
+
+    def last_ms(self) -> tuple[float, float, int]:
+        """(device ms of the whole call, ms from the last prompt position on, positions run)."""
+        t, d, n = ctypes.c_float(), ctypes.c_float(), ctypes.c_int32()
+        _lib.check(_lib.load().lc_batch_last_ms(self.handle, ctypes.byref(t), ctypes.byref(d), ctypes.byref(n)))
+        return float(t.value), float(d.value), int(n.value)
+
+    def logits(self, seq: int) -> np.ndarray:
+        """Logits of sequence `seq` at the last position of the last generate."""
+        out = np.zeros(self.model.cfg.vocab, np.float32)
+        _lib.check(_lib.load().lc_batch_logits(self.handle, int(seq), out.ctypes.data))
+        return out
+
+    def close(self) -> None:
+        self._fin()
+
+
 class LlamaInference:
     """Mirror of LlamaInference (LlamaInference.java): forward / generate / argmax."""
 

@@ -75,7 +75,7 @@ struct lc_context {
     int* d_err = nullptr;           // device error word of standalone kernels
     void* attn_scratch = nullptr;
     size_t attn_scratch_bytes = 0;
-    void* gemm_scratch = nullptr;   // row maxima, N-block tickets (zeroed), partial sums
+    void* gemm_scratch = nullptr;   // row scales, pre-split activations, partial sums
     size_t gemm_scratch_bytes = 0;
     bool gemm_ready = false;        // shared-memory attribute of the GEMM kernel set
 };
@@ -334,8 +334,7 @@ extern "C" int lc_gemm_f16_tiled(lc_context* c, const uint16_t* Wt, const float*
     auto* dY = (float*)s.arg(Y, (size_t)batch * rows * 4, kOut);
     if (s.status != LC_OK) return s.status;
     if (((uintptr_t)dW | (uintptr_t)dX | (uintptr_t)dY) & 15) return fail(LC_ERR_INVALID_ARG, "buffers must be 16-byte aligned");
-    const size_t nbk = (size_t)(rows + g.nblk - 1) / g.nblk;
-    const size_t off_t = 256, off_a = off_t + ((nbk * 4 + 255) / 256) * 256;
+    const size_t off_a = 256;
     const size_t off_p = off_a + ((gemm_split_bytes(batch, cols) + 255) / 256) * 256;
     const size_t need = off_p + gemm_part_bytes(g);
     if (c->gemm_scratch_bytes < need) {
@@ -356,7 +355,6 @@ extern "C" int lc_gemm_f16_tiled(lc_context* c, const uint16_t* Wt, const float*
     g.W = dW;
     g.As = As;
     g.unscale = unscale;
-    g.tickets = (uint32_t*)(base + off_t);
     g.part = (float*)(base + off_p);
     g.op = kGemmStore;
     g.y = dY;

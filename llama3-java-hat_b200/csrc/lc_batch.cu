@@ -109,10 +109,9 @@ struct BatchEngine {
     float *x = nullptr, *q = nullptr, *att = nullptr, *h = nullptr, *logits = nullptr, *unscale = nullptr;
     float *kcache = nullptr, *vcache = nullptr, *rope = nullptr, *part = nullptr;
     uint8_t* As = nullptr;
-    uint32_t* tickets = nullptr;
     unsigned long long* best = nullptr;
     int32_t *pos = nullptr, *seqlen = nullptr, *tok = nullptr, *nprompt = nullptr;
-    size_t part_bytes = 0, ticket_count = 0, attn_bytes = 0;
+    size_t part_bytes = 0, attn_bytes = 0;
     void* attn_scratch = nullptr;
     // per batch size: GEMM plans, tensor maps, graphs
     int gB = 0;
@@ -209,7 +208,7 @@ cudaError_t prepare(BatchEngine* e, int B) {
     base.err = e->err;
     base.timeout_ns = 2000000000ull;
     e->gp.assign(4 * m.n_layers + 1, base);
-    size_t part = 0, tickets = 0;
+    size_t part = 0;
     for (int j = 0; j < (int)e->gp.size(); ++j) {
         GemmParams& g = e->gp[j];
         const int l = j / 4, kind = j % 4;
@@ -265,7 +264,6 @@ cudaError_t prepare(BatchEngine* e, int B) {
         }
         if (!gemm_plan(&g, e->sms)) return cudaErrorInvalidValue;
         part = std::max(part, gemm_part_bytes(g));
-        tickets = std::max(tickets, (size_t)((g.N + g.nblk - 1) / g.nblk));
     }
     cudaError_t ce = cudaSuccess;
     if (part > e->part_bytes) {
@@ -275,15 +273,6 @@ cudaError_t prepare(BatchEngine* e, int B) {
         ce = cudaMalloc(&e->part, part);
         if (ce != cudaSuccess) return ce;
         e->part_bytes = part;
-    }
-    if (tickets > e->ticket_count) {
-        if (e->tickets) cudaFree(e->tickets);
-        e->tickets = nullptr;
-        e->ticket_count = 0;
-        ce = cudaMalloc(&e->tickets, tickets * 4);
-        if (ce == cudaSuccess) ce = cudaMemset(e->tickets, 0, tickets * 4);
-        if (ce != cudaSuccess) return ce;
-        e->ticket_count = tickets;
     }
     e->aplan = plan_attention(B, m.n_heads, m.n_kv, m.head_dim, m.max_seq, e->sms);
     const size_t ab = attention_scratch_bytes(e->aplan);
@@ -298,7 +287,6 @@ cudaError_t prepare(BatchEngine* e, int B) {
     e->wmap.resize(e->gp.size());
     for (size_t j = 0; j < e->gp.size(); ++j) {
         e->gp[j].part = e->part;
-        e->gp[j].tickets = e->tickets;
         ce = gemm_make_wmap(&e->wmap[j], e->gp[j]);
         if (ce != cudaSuccess) return ce;
     }
@@ -381,7 +369,7 @@ void batch_destroy(BatchEngine* e) {
     if (e->g_lm) cudaGraphExecDestroy(e->g_lm);
     if (e->g_nolm) cudaGraphExecDestroy(e->g_nolm);
     void* bufs[] = {e->x, e->q, e->att, e->h, e->logits, e->unscale, e->As, e->kcache, e->vcache, e->rope,
-                    e->best, e->pos, e->seqlen, e->nprompt, e->tok, e->part, e->tickets, e->attn_scratch};
+                    e->best, e->pos, e->seqlen, e->nprompt, e->tok, e->part, e->attn_scratch};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (e->ev0) cudaEventDestroy(e->ev0);

@@ -29,8 +29,8 @@
 //              lane 0 issues the MMAs of each chunk, commits them to the
 //              stage's "empty" barrier, and each unit to its accumulator;
 //   warps 2-5  epilogue: TMEM lane quarter warp % 4, 16 columns per load.
-// With kspl > 1 every unit writes its partial sums; the last unit of an N
-// block (ticket) adds them in split order (deterministic) and runs the
+// With kspl > 1 every unit writes its partial sums and a second, fully
+// parallel kernel adds them in split order (deterministic) and runs the
 // epilogue.  Every wait is bounded (error word + LC_ERR_TIMEOUT); TMEM is
 // released and in-flight copies and MMAs are drained on every path.
 #include <cudaTypedefs.h>
@@ -58,7 +58,6 @@ struct Bars {
     uint64_t dempty[2];       // accumulator read out (epilogue)
     uint64_t drain;           // all MMAs of the CTA done
     uint32_t tmem;
-    int flag;
     unsigned long long best[kGemmMaxB];
 };
 constexpr int kSmemMax = kRingBytes + (int)sizeof(Bars);
@@ -73,8 +72,9 @@ __device__ __forceinline__ void rope2(float& v0, float& v1, int pos, float freq)
     v1 = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
 }
 
-// Epilogue of output columns n..n+3 (n % 4 == 0) of row s.
-__device__ __forceinline__ void apply4(const GemmParams& p, Bars* bs, int s, int n, float (&y)[4]) {
+// Epilogue of output columns n..n+3 (n % 4 == 0) of row s.  Returns the
+// argmax key of the four logits (kGemmLogits; 0 otherwise).
+__device__ __forceinline__ unsigned long long apply4(const GemmParams& p, int s, int n, float (&y)[4]) {
     switch (p.op) {
         case kGemmStore:
             *reinterpret_cast<float4*>(p.y + (size_t)s * p.ldy + n) = make_float4(y[0], y[1], y[2], y[3]);
@@ -129,10 +129,10 @@ __device__ __forceinline__ void apply4(const GemmParams& p, Bars* bs, int s, int
                 else if (n + j == 0) kj = ~0ull;  // NaN at index 0: LlamaInference.argmax returns 0
                 k = kj > k ? kj : k;
             }
-            if (k) atomicMax(&bs->best[s], k);
-            break;
+            return k;
         }
     }
+    return 0ull;
 }
 
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ GemmParams p,
@@ -267,7 +267,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 #pragma unroll
                         for (int qd = 0; qd < 4; ++qd) {
                             float y4[4] = {y[4 * qd], y[4 * qd + 1], y[4 * qd + 2], y[4 * qd + 3]};
-                            apply4(p, bs, s, n0 + c0 + 4 * qd, y4);
+                            const unsigned long long k = apply4(p, s, n0 + c0 + 4 * qd, y4);
+                            if (k) atomicMax(&bs->best[s], k);
                         }
                     } else {
                         float4* dst = reinterpret_cast<float4*>(p.part + ((size_t)ks * p.B + s) * p.N + n0 + c0);
@@ -280,32 +281,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             tc_fence_before();
             named_bar_sync(kBarEpi, 128);
             if (et == 0) mbar_arrive(&bs->dempty[a]);
-            if (p.kspl > 1) {
-                // The last split of this N block adds the partials in split order.
-                __threadfence();
-                named_bar_sync(kBarEpi, 128);
-                if (et == 0) bs->flag = atomicAdd(p.tickets + nbi, 1u) == (uint32_t)(p.kspl - 1) ? 1 : 0;
-                named_bar_sync(kBarEpi, 128);
-                if (*reinterpret_cast<volatile int*>(&bs->flag)) {
-                    __threadfence();
-                    const int nq = nb >> 2;
-                    for (int i = et; i < p.B * nq; i += 128) {
-                        const int ss = i / nq, n = n0 + 4 * (i % nq);
-                        float4 acc = __ldcg(reinterpret_cast<const float4*>(p.part + (size_t)ss * p.N + n));
-                        for (int k = 1; k < p.kspl; ++k) {
-                            const float4 t =
-                                __ldcg(reinterpret_cast<const float4*>(p.part + ((size_t)k * p.B + ss) * p.N + n));
-                            acc.x += t.x;
-                            acc.y += t.y;
-                            acc.z += t.z;
-                            acc.w += t.w;
-                        }
-                        float y4[4] = {acc.x, acc.y, acc.z, acc.w};
-                        apply4(p, bs, ss, n, y4);
-                    }
-                    if (et == 0) p.tickets[nbi] = 0u;
-                }
-            }
             named_bar_sync(kBarEpi, 128);
             if (et < p.B && p.op == kGemmLogits && bs->best[et]) atomicMax(p.best + et, bs->best[et]);
             named_bar_sync(kBarEpi, 128);
@@ -316,6 +291,49 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+// Split-K results: y = the partial sums of the kspl splits added in split
+// order (deterministic), then the epilogue.  One (row, 4 columns) item per
+// thread; a row's items are consecutive, so the argmax keys of a warp are
+// merged before one atomic per row and warp.
+__global__ void __launch_bounds__(256) gemm_reduce_kernel(const __grid_constant__ GemmParams p) {
+    const int nq = p.N >> 2;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool live = i < (long long)p.B * nq;
+    int s = 0;
+    unsigned long long k = 0ull;
+    if (live) {
+        s = (int)(i / nq);
+        const int n = (int)(i % nq) * 4;
+        const float* src = p.part + (size_t)s * p.N + n;
+        const size_t stride = (size_t)p.B * p.N;
+        float4 acc = __ldcg(reinterpret_cast<const float4*>(src));
+        for (int ks = 1; ks < p.kspl; ++ks) {
+            const float4 t = __ldcg(reinterpret_cast<const float4*>(src + ks * stride));
+            acc.x += t.x;
+            acc.y += t.y;
+            acc.z += t.z;
+            acc.w += t.w;
+        }
+        float y4[4] = {acc.x, acc.y, acc.z, acc.w};
+        k = apply4(p, s, n, y4);
+    }
+    if (p.op == kGemmLogits) {
+        // lanes of one row are contiguous: reduce per (warp, row) segment
+        const int lane = threadIdx.x & 31;
+        const int s0 = __shfl_sync(0xffffffffu, s, 0);
+        const bool uniform = __all_sync(0xffffffffu, s == s0);
+        if (uniform) {
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, k, o);
+                k = k2 > k ? k2 : k;
+            }
+            if (lane == 0 && k) atomicMax(p.best + s0, k);
+        } else if (live && k) {
+            atomicMax(p.best + s, k);
+        }
+    }
 }
 
 // One activation row per CTA: max |A[s][k]|, the row scale 2^e with
@@ -371,8 +389,10 @@ bool gemm_plan(GemmParams* p, int num_sms) {
             // Per-CTA time of the slowest wave in bytes: weights (HBM), the
             // pre-split activations (L2, cheaper), a fixed cost per unit
             // (pipeline fill, epilogue) and the partial round trip of splits.
-            double cost = waves * (((double)nblk * krange * 2 + 0.35 * nrg * krange * 16) / bw + 48 * 1024);
-            if (kspl > 1) cost += 0.5 * (double)kspl * p->B * nblk * 4 + 24 * 1024;
+            double cost = waves * (((double)nblk * krange * 2 + 0.5 * nrg * krange * 16) / bw + 96 * 1024);
+            // Split K: partials written and read back by the reduce kernel
+            // (spread over the SMs) plus its launch.
+            if (kspl > 1) cost += 3.0 * (double)kspl * p->B * p->N * 4 / G + 128 * 1024;
             if (cost < best * 0.999) {
                 best = cost;
                 p->nblk = nblk;
@@ -454,6 +474,10 @@ cudaError_t launch_gemm(const GemmParams& p, const CUtensorMap& wmap, const CUte
     const int grid = p.units < num_sms ? p.units : num_sms;
     const int smem = p.stages * p.stage_bytes + (int)sizeof(Bars);
     gemm_kernel<<<grid, kThreads, smem, st>>>(p, wmap, amap);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || p.kspl == 1) return e;
+    const long long items = (long long)p.B * (p.N >> 2);
+    gemm_reduce_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(p);
     return cudaGetLastError();
 }
 

@@ -202,7 +202,6 @@ struct GemmParams {
     int nblk, kspl, units;  // N-block rows, K splits, (N-blocks) * kspl
     int stages, stage_bytes;
     float* part;             // [kspl][B][N] partial sums when kspl > 1
-    uint32_t* tickets;       // [N-blocks], zero between launches, when kspl > 1
     int op;
     float* y;
     int ldy;

@@ -167,6 +167,15 @@ int lc_attention_decode_static(lc_context* ctx, const float* q, const float* k, 
                                const int32_t* seq_len, int batch, int n_heads, int n_kv_heads, int head_dim,
                                int64_t seq_stride, int64_t head_stride, int64_t pos_stride);
 
+/* lc_attention_decode with the split plan sized for max_len, an upper bound
+ * of every seq_len[b] (positions past max_len are not attended).  seq_len is
+ * not read on the host, so with device buffers the call only enqueues (it
+ * can be captured in a CUDA graph); the first call of a context, or one with
+ * a larger plan, allocates scratch. */
+int lc_attention_decode_maxlen(lc_context* ctx, const float* q, const float* k, const float* v, float* out,
+                               const int32_t* seq_len, int batch, int n_heads, int n_kv_heads, int head_dim,
+                               int64_t seq_stride, int64_t head_stride, int64_t pos_stride, int max_len);
+
 /* LlamaInference.argmax(values) H/LlamaInference.java:252-262: first index of
  * the maximum (ties -> lowest index; 0 when values[0] is NaN). */
 int lc_argmax(lc_context* ctx, const float* values, int n, int32_t* out_index);

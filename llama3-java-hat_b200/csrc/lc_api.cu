@@ -530,6 +530,39 @@ extern "C" int lc_attention_decode(lc_context* c, const float* q, const float* k
     return s.finish(e);
 }
 
+extern "C" int lc_attention_decode_maxlen(lc_context* c, const float* q, const float* k, const float* v, float* out,
+                                          const int32_t* seq_len, int batch, int n_heads, int n_kv_heads,
+                                          int head_dim, int64_t seq_stride, int64_t head_stride, int64_t pos_stride,
+                                          int max_len) {
+    CTX_CHECK(c);
+    if (batch <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || max_len < 1)
+        return fail(LC_ERR_INVALID_ARG, "batch=%d n_heads=%d n_kv_heads=%d max_len=%d", batch, n_heads, n_kv_heads, max_len);
+    if (head_dim != kAttnHeadDim) return fail(LC_ERR_UNSUPPORTED, "fused attention implements head_dim 64, got %d", head_dim);
+    if (n_heads / n_kv_heads > 8) return fail(LC_ERR_UNSUPPORTED, "at most 8 query heads per kv head");
+    if ((seq_stride | head_stride | pos_stride) & 3) return fail(LC_ERR_INVALID_ARG, "strides must be multiples of 4 floats");
+    const size_t kv_floats = (size_t)(batch - 1) * seq_stride + (size_t)(n_kv_heads - 1) * head_stride +
+                             (size_t)(max_len - 1) * pos_stride + head_dim;
+    Stager s(c);
+    auto* dq = (const float*)s.arg(q, (size_t)batch * n_heads * head_dim * 4, kIn);
+    auto* dk = (const float*)s.arg(k, kv_floats * 4, kIn);
+    auto* dv = (const float*)s.arg(v, kv_floats * 4, kIn);
+    auto* dout = (float*)s.arg(out, (size_t)batch * n_heads * head_dim * 4, kOut);
+    auto* dl = (const int32_t*)s.arg(seq_len, (size_t)batch * 4, kIn);
+    if (s.status != LC_OK) return s.status;
+    if (((uintptr_t)dq | (uintptr_t)dk | (uintptr_t)dv) & 15) return fail(LC_ERR_INVALID_ARG, "q/k/v must be 16-byte aligned");
+    AttnPlan plan = plan_attention(batch, n_heads, n_kv_heads, head_dim, max_len, c->sms);
+    const size_t need = attention_scratch_bytes(plan);
+    if (c->attn_scratch_bytes < need) {
+        if (c->attn_scratch) cudaFree(c->attn_scratch);
+        c->attn_scratch = nullptr;
+        c->attn_scratch_bytes = 0;
+        CK(cudaMalloc(&c->attn_scratch, need), "attention scratch");
+        c->attn_scratch_bytes = need;
+    }
+    return s.finish(launch_attention_decode(plan, dq, dk, dv, dout, dl, seq_stride, head_stride, pos_stride,
+                                            c->attn_scratch, c->stream));
+}
+
 extern "C" int lc_argmax(lc_context* c, const float* values, int n, int32_t* out_index) {
     CTX_CHECK(c);
     if (n <= 0 || !out_index) return fail(LC_ERR_INVALID_ARG, "n=%d out=%p", n, (void*)out_index);

@@ -99,6 +99,8 @@ SIGNATURES = {
     "lc_attn_values": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]),
     "lc_attention_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
                                     c_int, c_int, c_int64, c_int64, c_int64]),
+    "lc_attention_decode_maxlen": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                           c_int, c_int, c_int, c_int64, c_int64, c_int64, c_int]),
     "lc_attention_decode_static": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                                            c_int, c_int, c_int, c_int64, c_int64, c_int64]),
     "lc_argmax": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),

@@ -278,6 +278,15 @@ class CudaAttention(_CudaKernel, IAttention):
             _addr(out, "f32", batch * n_heads * head_dim, True), _addr(seq_len, "i32", batch), batch, n_heads,
             n_kv_heads, head_dim, seq_stride, head_stride, pos_stride))
 
+    def decode_maxlen(self, q, k, v, out, seq_len, batch: int, n_heads: int, n_kv_heads: int, head_dim: int,
+                      seq_stride: int, head_stride: int, pos_stride: int, max_len: int) -> None:
+        """decode with the split plan sized for max_len >= every seq_len (see
+        lc_attention_decode_maxlen): enqueue-only with device buffers."""
+        _lib.check(self.lib.lc_attention_decode_maxlen(
+            self.ctx, _addr(q, "f32", batch * n_heads * head_dim), _addr(k, "f32", 1), _addr(v, "f32", 1),
+            _addr(out, "f32", batch * n_heads * head_dim, True), _addr(seq_len, "i32", batch), batch, n_heads,
+            n_kv_heads, head_dim, seq_stride, head_stride, pos_stride, max_len))
+
 
 class CudaKernelFactory(IKernelFactory):
     """The B200 sibling of PlainJavaKernelFactory (PlainJavaKernelFactory.java:9-40)."""

@@ -22,6 +22,9 @@ headline line above):
                      rotated past 4x L2), RMSNorm / SwiGLU / RoPE / softmax
                      rows, GQA decode attention (batch 1 / 64, 128..8192
                      cached positions); device time of back-to-back calls
+  --suite lmshard    (torchrun, N GPUs) lm_head rows sharded over the ranks:
+                     logits slice on each GPU, then NCCL all-gather of the
+                     slices or all-reduce of packed argmax keys
 
 Multi-GPU (torchrun): one independent sequence per GPU (replicas, no
 collective on the data path); value = sequences x tokens / max-over-ranks time.
@@ -560,6 +563,105 @@ def run_kernels(args):
     return 0
 
 
+def run_lmshard(args):
+    """lm_head row-shard study: rank r of N owns rows shard_rows(vocab, N, r)
+    of the 128256 x 2048 lm_head, computes its logits slice on the tcgen05
+    product, then the ranks either all-gather the slices (NCCL) or
+    max-all-reduce one packed argmax key per sequence.  Device time of
+    back-to-back steps, max over ranks; compute and exchange reported apart."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import llamahat
+    from llamahat import CudaKernelFactory
+    from llamahat.shard import shard_rows
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    acc = llamahat.Accelerator(local)
+    gemv = CudaKernelFactory().createGEMV(acc)
+    st = torch.cuda.ExternalStream(acc.stream, device=torch.device("cuda", local))
+    V, D, L2 = 128256, 2048, 126 * 1024 * 1024
+    lo, hi = shard_rows(V, ws, rank)
+    n = hi - lo
+    wb = n * D * 2
+    ncopy = max(1, min(16, -(-4 * L2 // wb)))
+    torch.manual_seed(SEED + rank)
+    Ws = []
+    for _ in range(ncopy):
+        W = (torch.randn(n * D, device="cuda") * 0.02).half()
+        Wt = torch.empty(n * D, dtype=torch.int16, device="cuda")
+        gemv.tile(W.view(torch.int16), Wt, n, D)
+        Ws.append(Wt)
+    torch.cuda.synchronize()
+    sign = -(1 << 63)
+    res = {}
+    for B in (1, 64):
+        torch.manual_seed(SEED)
+        X = torch.randn(B, D, device="cuda")
+        Y = torch.empty(B, n, device="cuda")
+        G = torch.empty(ws * B * n, device="cuda")
+        K = torch.empty(B, dtype=torch.int64, device="cuda")
+        it = [0]
+
+        def compute():
+            gemv.apply_batched_tiled(Ws[it[0] % ncopy], X, Y, n, D, B)
+            it[0] += 1
+
+        def gather():
+            with torch.cuda.stream(st):
+                if ws > 1:
+                    dist.all_gather_into_tensor(G, Y.view(-1))
+                else:
+                    G.copy_(Y.view(-1))
+
+        def keyreduce():
+            with torch.cuda.stream(st):
+                K.bitwise_xor_(sign)  # unsigned key order -> signed order
+                if ws > 1:
+                    dist.all_reduce(K, op=dist.ReduceOp.MAX)
+
+        def compute_key():
+            # the product's logits epilogue writes the slice's packed argmax keys
+            gemv.apply_batched_tiled_argmax(Ws[it[0] % ncopy], X, Y, n, D, B, lo, K)
+            it[0] += 1
+
+        cases = {"compute": [compute] * 16, "gather": [gather] * 16,
+                 "compute+gather": [lambda: (compute(), gather())] * 16,
+                 "compute_with_argmax_keys": [compute_key] * 16,
+                 "compute_with_argmax_keys+key_allreduce": [lambda: (compute_key(), keyreduce())] * 16}
+        for name, calls in cases.items():
+            us = device_us(calls, st)
+            t = torch.tensor([us], device="cuda")
+            if ws > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            res[f"B{B} {name}"] = float(t)
+        # consistency: the gathered argmax and the key reduce agree
+        compute_key()
+        gather()
+        keyreduce()
+        torch.cuda.synchronize()
+        full = G.view(ws, B, n).permute(1, 0, 2).reshape(B, ws * n)[:, :V]
+        idx_full = full.argmax(dim=1)
+        idx_key = (~(K & 0xFFFFFFFF)) & 0xFFFFFFFF
+        assert torch.equal(idx_full.cpu(), idx_key.cpu()), "gathered argmax != key all-reduce"
+    if rank == 0:
+        peak, kind = measured_peak()
+        line = {"suite": "lmshard", "metric": "lm_head row-shard step, us (max over ranks)", "n_gpus": ws,
+                "rows_per_gpu": n, "bytes_per_gpu": wb, "weight_copies": ncopy, "us": res,
+                "compute_GB_s_per_gpu": {f"B{B}": (wb + B * (n + D) * 4) / (res[f'B{B} compute'] * 1e-6) / 1e9
+                                         for B in (1, 64)},
+                "peak_GB_s": peak, "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({kind})",
+                "exchange": "NCCL all_gather_into_tensor of the fp32 slices; or all_reduce(MAX) of one int64 key "
+                            "per sequence", "scaling": "strong"}
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -568,7 +670,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
-    ap.add_argument("--suite", choices=["headline", "serving", "kernels"], default="headline")
+    ap.add_argument("--suite", choices=["headline", "serving", "kernels", "lmshard"], default="headline")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -576,6 +678,8 @@ def main():
         return run_serving(args)
     if args.suite == "kernels":
         return run_kernels(args)
+    if args.suite == "lmshard":
+        return run_lmshard(args)
     return run_ours(args)
 
 

@@ -96,6 +96,17 @@ int lc_weights_tile(lc_context* ctx, const uint16_t* W, uint16_t* Wt, int rows, 
  * products are exact and accumulate in fp32. */
 int lc_gemm_f16_tiled(lc_context* ctx, const uint16_t* Wt, const float* X, float* Y, int rows, int cols, int batch);
 
+/* lc_gemm_f16_tiled as a logits slice with its argmax: Y (may be NULL) as
+ * above, and keys[b] = the packed argmax of Y[b] -- order-preserving float
+ * bits in the high 32 bits, ~(index_offset + column) in the low 32, so the
+ * largest key is the first maximum (LlamaInference.argmax,
+ * H/LlamaInference.java:252-262; a NaN at global index 0 gives the largest
+ * key, other NaNs never win).  Keys of row slices held by different GPUs
+ * combine with an unsigned max (e.g. an all-reduce), which is how a
+ * row-sharded lm_head finds the next token without gathering logits. */
+int lc_gemm_f16_tiled_argmax(lc_context* ctx, const uint16_t* Wt, const float* X, float* Y, int rows, int cols,
+                             int batch, int32_t index_offset, uint64_t* keys);
+
 /* IRMSNorm.apply(x, weight, size) K/IRMSNorm.java:17; K/RMSNorm.java:35-50.
  * In place, eps = 1e-5f (K/RMSNorm.java:22). */
 int lc_rmsnorm(lc_context* ctx, float* x, const float* weight, int size);

@@ -315,8 +315,8 @@ extern "C" int lc_weights_tile(lc_context* c, const uint16_t* W, uint16_t* Wt, i
     return s.finish(launch_tile_rows(dW, dT, rows, cols, gemm_tile_width(cols), 0, 1, c->stream));
 }
 
-extern "C" int lc_gemm_f16_tiled(lc_context* c, const uint16_t* Wt, const float* X, float* Y, int rows, int cols,
-                                 int batch) {
+static int gemm_tiled(lc_context* c, const uint16_t* Wt, const float* X, float* Y, int rows, int cols, int batch,
+                      int idx_offset, uint64_t* keys) {
     CTX_CHECK(c);
     if (rows <= 0 || cols <= 0 || batch <= 0 || batch > kGemmMaxB || rows % 16 || gemm_tile_width(cols) == 0)
         return fail(LC_ERR_INVALID_ARG, "rows=%d cols=%d batch=%d (rows %% 16 == 0, cols %% 64 == 0, batch 1..%d)",
@@ -331,7 +331,8 @@ extern "C" int lc_gemm_f16_tiled(lc_context* c, const uint16_t* Wt, const float*
     Stager s(c);
     auto* dW = (const __half*)s.arg(Wt, (size_t)rows * cols * 2, kIn);
     auto* dX = (const float*)s.arg(X, (size_t)batch * cols * 4, kIn);
-    auto* dY = (float*)s.arg(Y, (size_t)batch * rows * 4, kOut);
+    auto* dY = Y ? (float*)s.arg(Y, (size_t)batch * rows * 4, kOut) : nullptr;
+    auto* dK = keys ? (unsigned long long*)s.arg(keys, (size_t)batch * 8, kOut) : nullptr;
     if (s.status != LC_OK) return s.status;
     if (((uintptr_t)dW | (uintptr_t)dX | (uintptr_t)dY) & 15) return fail(LC_ERR_INVALID_ARG, "buffers must be 16-byte aligned");
     const size_t off_a = 256;
@@ -356,18 +357,40 @@ extern "C" int lc_gemm_f16_tiled(lc_context* c, const uint16_t* Wt, const float*
     g.As = As;
     g.unscale = unscale;
     g.part = (float*)(base + off_p);
-    g.op = kGemmStore;
-    g.y = dY;
-    g.ldy = rows;
+    if (dK) {
+        g.op = kGemmLogits;
+        g.logits = dY;
+        g.ldl = rows;
+        g.best = dK;
+        g.idx_offset = idx_offset;
+    } else {
+        g.op = kGemmStore;
+        g.y = dY;
+        g.ldy = rows;
+    }
     g.n_valid = rows;
     g.err = c->d_err;
     g.timeout_ns = 2000000000ull;
     CUtensorMap wmap, amap;
     if (gemm_make_wmap(&wmap, g) != cudaSuccess || gemm_make_amap(&amap, g) != cudaSuccess)
         return fail(LC_ERR_CUDA, "tensor map encoding failed");
-    cudaError_t e = launch_gemm_split(dX, cols, cols, batch, As, unscale, c->stream);
+    cudaError_t e = dK ? cudaMemsetAsync(dK, 0, (size_t)batch * 8, c->stream) : cudaSuccess;
+    if (e == cudaSuccess) e = launch_gemm_split(dX, cols, cols, batch, As, unscale, c->stream);
     if (e == cudaSuccess) e = launch_gemm(g, wmap, amap, c->sms, c->stream);
     return s.finish(e);
+}
+
+extern "C" int lc_gemm_f16_tiled(lc_context* c, const uint16_t* Wt, const float* X, float* Y, int rows, int cols,
+                                 int batch) {
+    if (!Y) return fail(LC_ERR_INVALID_ARG, "NULL buffer");
+    return gemm_tiled(c, Wt, X, Y, rows, cols, batch, 0, nullptr);
+}
+
+extern "C" int lc_gemm_f16_tiled_argmax(lc_context* c, const uint16_t* Wt, const float* X, float* Y, int rows,
+                                        int cols, int batch, int32_t index_offset, uint64_t* keys) {
+    if (!keys) return fail(LC_ERR_INVALID_ARG, "NULL keys");
+    if (index_offset < 0) return fail(LC_ERR_INVALID_ARG, "index_offset %d", index_offset);
+    return gemm_tiled(c, Wt, X, Y, rows, cols, batch, index_offset, keys);
 }
 
 extern "C" int lc_rmsnorm_rows(lc_context* c, float* x, const float* w, int rows, int width, float eps) {

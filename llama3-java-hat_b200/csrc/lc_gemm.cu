@@ -125,8 +125,8 @@ __device__ __forceinline__ unsigned long long apply4(const GemmParams& p, int s,
             for (int j = 0; j < 4; ++j) {
                 unsigned long long kj = 0;
                 if (n + j >= p.n_valid) break;
-                if (y[j] == y[j]) kj = argmax_key(y[j], n + j);
-                else if (n + j == 0) kj = ~0ull;  // NaN at index 0: LlamaInference.argmax returns 0
+                if (y[j] == y[j]) kj = argmax_key(y[j], p.idx_offset + n + j);
+                else if (p.idx_offset + n + j == 0) kj = ~0ull;  // NaN at index 0: LlamaInference.argmax returns 0
                 k = kj > k ? kj : k;
             }
             return k;

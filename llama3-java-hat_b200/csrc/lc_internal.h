@@ -220,6 +220,7 @@ struct GemmParams {
     float* logits;
     int ldl;
     int n_valid;              // columns >= n_valid are padding (kGemmLogits)
+    int idx_offset;           // global index of column 0 in the argmax keys (kGemmLogits)
     unsigned long long* best; // [B]
     int* err;
     uint64_t timeout_ns;

@@ -80,6 +80,8 @@ SIGNATURES = {
     "lc_gemv_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int]),
     "lc_gemv_f16_batched": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int]),
     "lc_weights_tile": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int]),
+    "lc_gemm_f16_tiled_argmax": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int32,
+                                         c_void_p]),
     "lc_batch_create": (c_int, [c_void_p, c_int32, POINTER(c_void_p)]),
     "lc_batch_destroy": (c_int, [c_void_p]),
     "lc_batch_generate": (c_int, [c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_void_p]),

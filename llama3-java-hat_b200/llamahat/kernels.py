@@ -203,6 +203,23 @@ class CudaGEMV(_CudaKernel, IGEMV):
         _lib.check(self.lib.lc_weights_tile(self.ctx, _addr(matrix, "f16", n), _addr(tiled, "f16", n, writable=True),
                                             rows, cols))
 
+    def apply_batched_tiled_argmax(self, tiled, X, Y, rows: int, cols: int, batch: int, index_offset: int,
+                                   keys) -> None:
+        """apply_batched_tiled plus packed argmax keys per row (keys: uint64 /
+        int64 buffer of `batch`; Y may be None)."""
+        y = None if Y is None else _addr(Y, "f32", batch * rows, writable=True)
+        if isinstance(keys, np.ndarray):
+            if keys.dtype not in (np.uint64, np.int64) or keys.size < batch:
+                raise TypeError("keys must be a uint64/int64 array of `batch` entries")
+            k = keys.ctypes.data
+        else:
+            if str(keys.dtype) not in ("torch.int64", "torch.uint64") or keys.numel() < batch:
+                raise TypeError("keys must be an int64 tensor of `batch` entries")
+            k = keys.data_ptr()
+        _lib.check(self.lib.lc_gemm_f16_tiled_argmax(self.ctx, _addr(tiled, "f16", rows * cols),
+                                                     _addr(X, "f32", batch * cols), y, rows, cols, batch,
+                                                     int(index_offset), k))
+
     def apply_batched_tiled(self, tiled, X, Y, rows: int, cols: int, batch: int) -> None:
         """Y[b] = W @ X[b] for b < batch <= 64 on the tcgen05 tensor cores; W
         given in the tiled layout (`tile`)."""

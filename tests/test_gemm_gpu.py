@@ -80,6 +80,33 @@ def test_gemm_device_buffers_and_repeat(gemv, oracle):
     assert_kernel_close(y1[3], oracle.gemv_f16(W, X[3]))
 
 
+@pytest.mark.parametrize("batch,offset", [(1, 0), (5, 1000), (64, 64128)])
+def test_gemm_argmax_keys(gemv, oracle, batch, offset):
+    """Packed argmax keys of the logits epilogue: the first maximum of each
+    row (LlamaInference.argmax), global index = offset + column; a planted tie
+    resolves to the lower column."""
+    rows, cols = 4096, 2048
+    rng = np.random.default_rng(batch + offset)
+    W = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float16)
+    W[1000] = W[3000]  # identical rows: equal logits, column 1000 must win
+    X = rng.standard_normal((batch, cols)).astype(f32)
+    X[0] = W[3000].astype(f32) * 50  # make row 1000 / 3000 the maximum of sequence 0
+    Wt = _tiled(gemv, W)
+    Y = np.zeros((batch, rows), f32)
+    keys = np.zeros(batch, np.uint64)
+    gemv.apply_batched_tiled_argmax(Wt, X, Y, rows, cols, batch, offset, keys)
+    idx = (~(keys & np.uint64(0xFFFFFFFF))) & np.uint64(0xFFFFFFFF)
+    for b in range(batch):
+        first = int(np.argmax(Y[b]))  # numpy: first maximum of the GPU logits
+        assert int(idx[b]) == offset + first
+    assert int(idx[0]) == offset + 1000
+    assert_kernel_close(Y[0], oracle.gemv_f16(W, X[0]))
+    # without logits
+    k2 = np.zeros(batch, np.uint64)
+    gemv.apply_batched_tiled_argmax(Wt, X, None, rows, cols, batch, offset, k2)
+    assert np.array_equal(keys, k2)
+
+
 def test_gemm_rejects_bad_shapes(gemv):
     from llamahat import IllegalArgumentError
     W = np.zeros(64 * 64, np.float16)

@@ -37,6 +37,7 @@ size_t attention_scratch_bytes(const AttnPlan& p) {
     return ((parts + 255) / 256) * 256 + cnts;
 }
 
+template <int KVM>
 __global__ void __launch_bounds__(256) attention_decode_kernel(const float* __restrict__ q, const float* __restrict__ k,
                                                                const float* __restrict__ v, float* __restrict__ out,
                                                                const int32_t* __restrict__ seq_len, int n_heads,
@@ -63,7 +64,7 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(const float* __re
     const float* kb = k + (int64_t)b * seq_stride + (int64_t)h * head_stride;
     const float* vb = v + (int64_t)b * seq_stride + (int64_t)h * head_stride;
     float* pb = part + ((int64_t)b * n_kv + h) * max_splits * kv_mul * kAttnPartStride;
-    attention_unit(qh, kb, vb, pos_stride, t0, t1, nsplit, s, o, pb, cnt + (int64_t)b * n_kv + h, scale, kv_mul,
+    attention_unit<KVM>(qh, kb, vb, pos_stride, t0, t1, nsplit, s, o, pb, cnt + (int64_t)b * n_kv + h, scale, kv_mul,
                    split_len, sm);
 }
 
@@ -78,15 +79,28 @@ cudaError_t launch_attention_decode(const AttnPlan& p, const float* q, const flo
     cudaError_t e = cudaMemsetAsync(cnt, 0, (size_t)p.batch * p.n_kv * sizeof(uint32_t), st);
     if (e != cudaSuccess) return e;
     const size_t smem = (size_t)attn_unit_smem_floats(kv_mul, p.split_len) * sizeof(float);
-    if (smem > 48 * 1024) {
-        e = cudaFuncSetAttribute(attention_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
     const float scale = 1.0f / (float)sqrt((double)p.head_dim);  // Attention.java:33
     const long long grid = (long long)p.batch * p.n_kv * p.max_splits;
-    attention_decode_kernel<<<(unsigned)grid, 256, smem, st>>>(q, k, v, out, seq_len, p.n_heads, p.n_kv, seq_stride,
-                                                               head_stride, pos_stride, p.split_len, p.max_splits,
-                                                               part, cnt, scale);
+    // The throughput path is compiled for 1, 2, 4 and 8 query heads per kv
+    // head (register arrays sized at compile time); other ratios use the
+    // exact path at every length.
+    auto run = [&](auto kern) -> cudaError_t {
+        if (smem > 48 * 1024) {
+            cudaError_t a = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (a != cudaSuccess) return a;
+        }
+        kern<<<(unsigned)grid, 256, smem, st>>>(q, k, v, out, seq_len, p.n_heads, p.n_kv, seq_stride, head_stride,
+                                                pos_stride, p.split_len, p.max_splits, part, cnt, scale);
+        return cudaSuccess;
+    };
+    switch (kv_mul) {
+        case 1: e = run(attention_decode_kernel<1>); break;
+        case 2: e = run(attention_decode_kernel<2>); break;
+        case 4: e = run(attention_decode_kernel<4>); break;
+        case 8: e = run(attention_decode_kernel<8>); break;
+        default: e = run(attention_decode_kernel<0>); break;
+    }
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

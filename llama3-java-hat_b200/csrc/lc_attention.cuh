@@ -21,9 +21,13 @@ namespace lc {
 
 constexpr int kAttnHeadDim = 64;
 
-// Shared-memory floats a unit needs.
+// Units of more than kAttnExactMax positions take the throughput path.
+constexpr int kAttnExactMax = 64;
+
+// Shared-memory floats a unit needs: q, scores, (max, sum) per head and a
+// flag word, then the cross-warp value partials of the throughput path.
 __host__ __device__ inline int attn_unit_smem_floats(int kv_mul, int tmax) {
-    return kv_mul * kAttnHeadDim + kv_mul * tmax + 2 * kv_mul + 4;
+    return kv_mul * kAttnHeadDim + kv_mul * tmax + 2 * kv_mul + 4 + (tmax > kAttnExactMax ? 8 * kv_mul * kAttnHeadDim : 0);
 }
 
 // Partial record per (split, head): [m, l, o[64]].
@@ -115,8 +119,137 @@ __device__ __forceinline__ void attention_core(const float* __restrict__ q, cons
     }
 }
 
-// Standalone unit: attention_core, then with several splits the last unit to
-// finish (ticket on *cnt) merges the partials into out.
+// Throughput form of attention_core for units of more than kAttnExactMax
+// positions: the same results up to float rounding (exp in float, sums in a
+// tree order), with K and V rows read once, fully coalesced.  Scores: each
+// warp takes 4 positions at a time, 8 lanes per position holding 8 of the
+// 64 dimensions, a 3-step shuffle per head.  Softmax: one warp per head.
+// Values: warps take positions t = warp (mod 8), each lane 2 dimensions of
+// every head; the 8 warp partials are added in shared memory.
+template <int KVM>
+__device__ __forceinline__ void attention_core_fast(const float* __restrict__ q, const float* __restrict__ K,
+                                                    const float* __restrict__ Vc, int64_t pos_stride, int t0,
+                                                    int t1, int nsplit, int split, float* __restrict__ out,
+                                                    float* __restrict__ part, int part_stride, float scale,
+                                                    int tmax, float* sm) {
+    constexpr int HD = kAttnHeadDim, MAXH = KVM, kv_mul = KVM;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 3, sub = lane & 7;
+    const int T = t1 - t0;
+    float* qs = sm;
+    float* sc = qs + kv_mul * HD;
+    float* st = sc + kv_mul * tmax;
+    float* red = st + 2 * kv_mul + 4;  // [8 warps][kv_mul][64]
+
+    for (int i = tid; i < kv_mul * HD; i += 256) qs[i] = __ldcg(q + i);
+    named_bar_sync(1, 256);
+    float qr[MAXH][8];
+#pragma unroll
+    for (int h = 0; h < MAXH; ++h)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) qr[h][j] = h < kv_mul ? qs[h * HD + 8 * sub + j] : 0.0f;
+
+    // Scores, two rounds of 32 positions in flight per warp pass.
+    for (int base = warp * 4; base < T; base += 64) {
+        float4 a[2], b[2];
+        bool ok[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int t = base + 32 * r + g;
+            ok[r] = t < T;
+            if (ok[r]) {
+                const float4* kr = reinterpret_cast<const float4*>(K + (int64_t)(t0 + t) * pos_stride) + 2 * sub;
+                a[r] = __ldcg(kr);
+                b[r] = __ldcg(kr + 1);
+            } else {
+                a[r] = b[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int t = base + 32 * r + g;
+#pragma unroll
+            for (int h = 0; h < MAXH; ++h) {
+                if (h < kv_mul) {
+                    float d = qr[h][0] * a[r].x;
+                    d = fmaf(qr[h][1], a[r].y, d);
+                    d = fmaf(qr[h][2], a[r].z, d);
+                    d = fmaf(qr[h][3], a[r].w, d);
+                    d = fmaf(qr[h][4], b[r].x, d);
+                    d = fmaf(qr[h][5], b[r].y, d);
+                    d = fmaf(qr[h][6], b[r].z, d);
+                    d = fmaf(qr[h][7], b[r].w, d);
+                    d += __shfl_xor_sync(0xffffffffu, d, 1);
+                    d += __shfl_xor_sync(0xffffffffu, d, 2);
+                    d += __shfl_xor_sync(0xffffffffu, d, 4);
+                    if (sub == 0 && ok[r]) sc[h * tmax + t] = d * scale;
+                }
+            }
+        }
+    }
+    named_bar_sync(1, 256);
+
+    // Per head: max, e = exp(s - max), sum.
+    for (int h = warp; h < kv_mul; h += 8) {
+        float* e = sc + h * tmax;
+        float m = -INFINITY;
+        for (int t = lane; t < T; t += 32) m = fmaxf(m, e[t]);
+        m = warp_max(m);
+        float l = 0.0f;
+        for (int t = lane; t < T; t += 32) {
+            const float v = expf(e[t] - m);
+            e[t] = v;
+            l += v;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            st[2 * h] = m;
+            st[2 * h + 1] = l;
+        }
+    }
+    named_bar_sync(1, 256);
+
+    // Weighted values.
+    float2 acc[MAXH];
+#pragma unroll
+    for (int h = 0; h < MAXH; ++h) acc[h] = make_float2(0.f, 0.f);
+#pragma unroll 4
+    for (int t = warp; t < T; t += 8) {
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(Vc + (int64_t)(t0 + t) * pos_stride) + lane);
+#pragma unroll
+        for (int h = 0; h < MAXH; ++h) {
+            if (h < kv_mul) {
+                const float p = sc[h * tmax + t];
+                acc[h].x = fmaf(p, v.x, acc[h].x);
+                acc[h].y = fmaf(p, v.y, acc[h].y);
+            }
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < MAXH; ++h)
+        if (h < kv_mul) reinterpret_cast<float2*>(red + (warp * kv_mul + h) * HD)[lane] = acc[h];
+    named_bar_sync(1, 256);
+    for (int hi = tid; hi < kv_mul * HD; hi += 256) {
+        const int h = hi / HD, i = hi % HD;
+        float o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) o += red[(w * kv_mul + h) * HD + i];
+        if (nsplit == 1) {
+            out[h * HD + i] = o * (1.0f / st[2 * h + 1]);
+        } else {
+            float* pp = part + ((int64_t)split * kv_mul + h) * part_stride;
+            pp[2 + i] = o;
+            if (i == 0) {
+                pp[0] = st[2 * h];
+                pp[1] = st[2 * h + 1];
+            }
+        }
+    }
+}
+
+// Standalone unit: attention_core (attention_core_fast<KVM> for units of
+// more than kAttnExactMax positions when KVM = kv_mul > 0), then with several
+// splits the last unit to finish (ticket on *cnt) merges the partials into out.
+template <int KVM>
 __device__ __forceinline__ void attention_unit(const float* __restrict__ q, const float* __restrict__ K,
                                                const float* __restrict__ Vc, int64_t pos_stride, int t0, int t1,
                                                int nsplit, int split, float* __restrict__ out,
@@ -124,7 +257,11 @@ __device__ __forceinline__ void attention_unit(const float* __restrict__ q, cons
                                                int tmax, float* sm) {
     constexpr int HD = kAttnHeadDim;
     const int tid = threadIdx.x;
-    attention_core(q, K, Vc, pos_stride, t0, t1, nsplit, split, out, part, kAttnPartStride, scale, kv_mul, tmax, sm);
+    if (KVM > 0 && tmax > kAttnExactMax)
+        attention_core_fast<(KVM > 0 ? KVM : 1)>(q, K, Vc, pos_stride, t0, t1, nsplit, split, out, part,
+                                                 kAttnPartStride, scale, tmax, sm);
+    else
+        attention_core(q, K, Vc, pos_stride, t0, t1, nsplit, split, out, part, kAttnPartStride, scale, kv_mul, tmax, sm);
     volatile int* flag = reinterpret_cast<volatile int*>(sm + kv_mul * HD + kv_mul * tmax + 2 * kv_mul);
     if (nsplit > 1) {
         __threadfence();

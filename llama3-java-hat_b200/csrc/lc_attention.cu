@@ -45,6 +45,8 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(const float* __re
                                                                int64_t pos_stride, int split_len, int max_splits,
                                                                float* part, uint32_t* cnt, float scale) {
     extern __shared__ float sm[];
+    griddep_launch();
+    griddep_wait();
     const int s = blockIdx.x % max_splits;
     const int h = (blockIdx.x / max_splits) % n_kv;
     const int b = blockIdx.x / (max_splits * n_kv);
@@ -70,13 +72,15 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(const float* __re
 
 cudaError_t launch_attention_decode(const AttnPlan& p, const float* q, const float* k, const float* v, float* out,
                                     const int32_t* seq_len, int64_t seq_stride, int64_t head_stride,
-                                    int64_t pos_stride, void* scratch, cudaStream_t st) {
+                                    int64_t pos_stride, void* scratch, cudaStream_t st, bool pdl) {
     const int kv_mul = p.n_heads / p.n_kv;
     size_t parts = (size_t)p.batch * p.n_kv * p.max_splits * kv_mul * kAttnPartStride * sizeof(float);
     parts = ((parts + 255) / 256) * 256;
     float* part = reinterpret_cast<float*>(scratch);
     uint32_t* cnt = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(scratch) + parts);
-    cudaError_t e = cudaMemsetAsync(cnt, 0, (size_t)p.batch * p.n_kv * sizeof(uint32_t), st);
+    // The merging unit leaves each counter at zero; a PDL launch (graph
+    // replays of a prepared plan) relies on that, other launches clear them.
+    cudaError_t e = pdl ? cudaSuccess : cudaMemsetAsync(cnt, 0, (size_t)p.batch * p.n_kv * sizeof(uint32_t), st);
     if (e != cudaSuccess) return e;
     const size_t smem = (size_t)attn_unit_smem_floats(kv_mul, p.split_len) * sizeof(float);
     const float scale = 1.0f / (float)sqrt((double)p.head_dim);  // Attention.java:33
@@ -89,9 +93,8 @@ cudaError_t launch_attention_decode(const AttnPlan& p, const float* q, const flo
             cudaError_t a = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             if (a != cudaSuccess) return a;
         }
-        kern<<<(unsigned)grid, 256, smem, st>>>(q, k, v, out, seq_len, p.n_heads, p.n_kv, seq_stride, head_stride,
-                                                pos_stride, p.split_len, p.max_splits, part, cnt, scale);
-        return cudaSuccess;
+        return launch_ex(kern, dim3((unsigned)grid), dim3(256), smem, st, pdl, q, k, v, out, seq_len, p.n_heads, p.n_kv,
+                         seq_stride, head_stride, pos_stride, p.split_len, p.max_splits, part, cnt, scale);
     };
     switch (kv_mul) {
         case 1: e = run(attention_decode_kernel<1>); break;

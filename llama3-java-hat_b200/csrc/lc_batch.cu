@@ -36,6 +36,8 @@ __global__ void __launch_bounds__(kNormThreads) norm_split_kernel(
     float* __restrict__ unscale, unsigned long long* __restrict__ best) {
     extern __shared__ float ys[];  // dim floats
     __shared__ float red[kNormThreads / 32];
+    griddep_launch();
+    griddep_wait();
     const int s = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float* xs = x + (size_t)s * dim;
     if (emb) {
@@ -85,6 +87,8 @@ __global__ void __launch_bounds__(kNormThreads) norm_split_kernel(
 __global__ void step_end_kernel(int B, int32_t* __restrict__ pos, int32_t* __restrict__ seqlen,
                                 int32_t* __restrict__ tok, int tok_stride, const int32_t* __restrict__ n_prompt,
                                 const unsigned long long* __restrict__ best, int lm) {
+    griddep_launch();
+    griddep_wait();
     const int s = threadIdx.x;
     if (s >= B) return;
     const int p = pos[s];
@@ -142,37 +146,38 @@ cudaError_t enqueue_step(BatchEngine* e, int B, bool lm) {
     const size_t layer_kv = (size_t)m.n_kv * m.max_seq * m.head_dim;
     const int64_t seq_stride = (int64_t)kv_floats_per_seq(m), head_stride = (int64_t)m.max_seq * m.head_dim;
     cudaError_t ce = cudaSuccess;
+    // Every launch of the step is a programmatic dependent of the one before
+    // (each kernel waits for its predecessor before touching its results).
+    constexpr bool pdl = true;
     auto norm = [&](const float* w, const __half* emb, unsigned long long* best) {
-        norm_split_kernel<<<B, kNormThreads, (size_t)m.dim * 4, e->st>>>(e->x, m.dim, w, m.eps, emb, e->tok,
-                                                                          e->tok_stride, e->pos, e->As, e->unscale,
-                                                                          best);
-        return cudaGetLastError();
+        return launch_ex(norm_split_kernel, dim3(B), dim3(kNormThreads), (size_t)m.dim * 4, e->st, pdl, e->x, m.dim,
+                         w, m.eps, emb, (const int32_t*)e->tok, e->tok_stride, (const int32_t*)e->pos, e->As,
+                         e->unscale, best);
     };
     for (int l = 0; l < m.n_layers && ce == cudaSuccess; ++l) {
         const LayerW& L = m.layers[l];
         const int j = 4 * l;
         ce = norm(L.attn_norm, l == 0 ? m.tok_emb : nullptr, nullptr);
-        if (ce == cudaSuccess) ce = launch_gemm(e->gp[j + kJobQKV], e->wmap[j + kJobQKV], e->amap_dim, e->sms, e->st);
+        if (ce == cudaSuccess) ce = launch_gemm(e->gp[j + kJobQKV], e->wmap[j + kJobQKV], e->amap_dim, e->sms, e->st, pdl);
         if (ce == cudaSuccess)
             ce = launch_attention_decode(e->aplan, e->q, e->kcache + l * layer_kv, e->vcache + l * layer_kv, e->att,
-                                         e->seqlen, seq_stride, head_stride, m.head_dim, e->attn_scratch, e->st);
-        if (ce == cudaSuccess) ce = launch_gemm_split(e->att, qdim, qdim, B, e->As, e->unscale, e->st);
-        if (ce == cudaSuccess) ce = launch_gemm(e->gp[j + kJobO], e->wmap[j + kJobO], e->amap_qdim, e->sms, e->st);
+                                         e->seqlen, seq_stride, head_stride, m.head_dim, e->attn_scratch, e->st, pdl);
+        if (ce == cudaSuccess) ce = launch_gemm_split(e->att, qdim, qdim, B, e->As, e->unscale, e->st, pdl);
+        if (ce == cudaSuccess) ce = launch_gemm(e->gp[j + kJobO], e->wmap[j + kJobO], e->amap_qdim, e->sms, e->st, pdl);
         if (ce == cudaSuccess) ce = norm(L.ffn_norm, nullptr, nullptr);
-        if (ce == cudaSuccess) ce = launch_gemm(e->gp[j + kJobGU], e->wmap[j + kJobGU], e->amap_dim, e->sms, e->st);
-        if (ce == cudaSuccess) ce = launch_gemm_split(e->h, m.hidden, m.hidden, B, e->As, e->unscale, e->st);
+        if (ce == cudaSuccess) ce = launch_gemm(e->gp[j + kJobGU], e->wmap[j + kJobGU], e->amap_dim, e->sms, e->st, pdl);
+        if (ce == cudaSuccess) ce = launch_gemm_split(e->h, m.hidden, m.hidden, B, e->As, e->unscale, e->st, pdl);
         if (ce == cudaSuccess)
-            ce = launch_gemm(e->gp[j + kJobDN], e->wmap[j + kJobDN], e->amap_hidden, e->sms, e->st);
+            ce = launch_gemm(e->gp[j + kJobDN], e->wmap[j + kJobDN], e->amap_hidden, e->sms, e->st, pdl);
     }
     const int jl = 4 * m.n_layers;
     if (lm && ce == cudaSuccess) {
         ce = norm(m.out_norm, nullptr, e->best);
-        if (ce == cudaSuccess) ce = launch_gemm(e->gp[jl], e->wmap[jl], e->amap_dim, e->sms, e->st);
+        if (ce == cudaSuccess) ce = launch_gemm(e->gp[jl], e->wmap[jl], e->amap_dim, e->sms, e->st, pdl);
     }
     if (ce == cudaSuccess) {
-        step_end_kernel<<<1, kGemmMaxB, 0, e->st>>>(B, e->pos, e->seqlen, e->tok, e->tok_stride, e->nprompt, e->best,
-                                                    lm ? 1 : 0);
-        ce = cudaGetLastError();
+        ce = launch_ex(step_end_kernel, dim3(1), dim3(kGemmMaxB), 0, e->st, pdl, B, e->pos, e->seqlen, e->tok,
+                       e->tok_stride, (const int32_t*)e->nprompt, (const unsigned long long*)e->best, lm ? 1 : 0);
     }
     return ce;
 }
@@ -284,6 +289,10 @@ cudaError_t prepare(BatchEngine* e, int B) {
         if (ce != cudaSuccess) return ce;
         e->attn_bytes = ab;
     }
+    // The graph's attention launches rely on zero completion counters (the
+    // merging unit leaves them at zero).
+    ce = cudaMemset(e->attn_scratch, 0, e->attn_bytes);
+    if (ce != cudaSuccess) return ce;
     e->wmap.resize(e->gp.size());
     for (size_t j = 0; j < e->gp.size(); ++j) {
         e->gp[j].part = e->part;

@@ -115,6 +115,17 @@ LC_DEV void prefetch_l2(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
+// ------------------------------------------- programmatic dependent launch --
+//
+// A kernel launched with programmatic stream serialisation may start while
+// its predecessor in the stream is still running.  griddep_wait() blocks
+// until the predecessor grid has completed and its memory operations are
+// visible; it returns at once when the kernel was launched normally.
+// griddep_launch() lets the dependent kernel be scheduled before this one
+// finishes (each dependent still waits for this grid's completion).
+LC_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+LC_DEV void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------ named CTA barriers --
 
 LC_DEV void named_bar_sync(uint32_t id, uint32_t nthreads) {

@@ -170,11 +170,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (lane == 0) {
             const uint64_t wpol = l2_policy_evict_first(), apol = l2_policy_evict_last();
             const uint32_t tx = (uint32_t)(p.nblk * kKC * 2 + nrg * 1024);  // full boxes, out-of-range rows zero-filled
-            uint32_t it = 0, slot = 0, par = 1;
+            // Weights never depend on an earlier kernel: the first stages'
+            // weight boxes go out before the wait for the predecessor (whose
+            // results the activation boxes carry).
+            const int u0 = blockIdx.x;
+            const int pre = u0 < p.units ? min(NS, nchunk) : 0;
+            {
+                const int ks = u0 % p.kspl, g0 = ((u0 / p.kspl) * p.nblk) >> 3;
+                for (int c = 0; c < pre; ++c) {
+                    const int kc = ks * krange + c * kKC;
+                    mbar_arrive_expect_tx(&bs->full[c], tx);
+                    tma_load_4d(smem + c * SB + kABytes, &wmap, 0, (kc % p.cbw) >> 3, kc / p.cbw, g0, &bs->full[c],
+                                wpol);
+                }
+            }
+            griddep_wait();
+            for (int c = 0; c < pre; ++c)
+                tma_load_3d(smem + c * SB, &amap, 0, ((u0 % p.kspl) * krange + c * kKC) >> 3, 0, &bs->full[c], apol);
+            uint32_t it = (uint32_t)pre, slot = (uint32_t)(pre % NS), par = pre == NS ? 0u : 1u;
             bool ok = true;
             for (int u = blockIdx.x; u < p.units && ok; u += G) {
                 const int ks = u % p.kspl, g0 = ((u / p.kspl) * p.nblk) >> 3;
-                for (int c = 0; c < nchunk; ++c) {
+                for (int c = (u == u0 ? pre : 0); c < nchunk; ++c) {
                     if (!mbar_wait_bounded(&bs->empty[slot], par, p.err, globaltimer_ns() + p.timeout_ns,
                                            kDevTimeoutEmpty)) {
                         ok = false;
@@ -240,11 +257,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
     } else {
         // -------------------------------------------------------- epilogue --
+        griddep_wait();  // unscale and the epilogue's outputs belong to the predecessor's stream order
         const int et = threadIdx.x - kEpiT0, q4 = warp & 3, r = q4 * 32 + lane, s = r >> 1;
         const bool lead = (r & 1) == 0 && s < p.B;
-        const float unscale = s < p.B ? __ldg(p.unscale + s) : 0.0f;
+        const float unscale = s < p.B ? __ldcg(p.unscale + s) : 0.0f;
         int j = 0;
         for (int u = blockIdx.x; u < p.units; u += G, ++j) {
+            // Dependents may launch once every CTA is in its last epilogue
+            // (earlier, their blocks would compete with the weight stream).
+            if (u + G >= p.units) griddep_launch();
             const int a = j & 1, nbi = u / p.kspl, ks = u % p.kspl, n0 = nbi * p.nblk, nb = min(p.nblk, p.N - n0);
             if (et < kGemmMaxB) bs->best[et] = 0ull;
             bool got = mbar_wait_bounded(&bs->dfull[a], (j >> 1) & 1, p.err, globaltimer_ns() + p.timeout_ns,
@@ -298,6 +319,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 // thread; a row's items are consecutive, so the argmax keys of a warp are
 // merged before one atomic per row and warp.
 __global__ void __launch_bounds__(256) gemm_reduce_kernel(const __grid_constant__ GemmParams p) {
+    griddep_launch();
+    griddep_wait();
     const int nq = p.N >> 2;
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const bool live = i < (long long)p.B * nq;
@@ -342,6 +365,8 @@ __global__ void __launch_bounds__(256) gemm_reduce_kernel(const __grid_constant_
 // group s / 4).
 __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ A, int lda, int K,
                                                          uint8_t* __restrict__ As, float* __restrict__ unscale) {
+    griddep_launch();
+    griddep_wait();
     const int s = blockIdx.x;
     const float* a = A + (size_t)s * lda;
     float m = 0.0f;
@@ -467,23 +492,21 @@ cudaError_t gemm_make_amap(CUtensorMap* out, const GemmParams& p) {
 }
 
 cudaError_t launch_gemm(const GemmParams& p, const CUtensorMap& wmap, const CUtensorMap& amap, int num_sms,
-                        cudaStream_t st) {
+                        cudaStream_t st, bool pdl) {
     if (p.stages < 2 || p.stages > kMaxStages || p.stages * p.stage_bytes > kRingBytes || p.nblk % 16 ||
         p.nblk > kMaxN || p.units < 1)
         return cudaErrorInvalidValue;
     const int grid = p.units < num_sms ? p.units : num_sms;
     const int smem = p.stages * p.stage_bytes + (int)sizeof(Bars);
-    gemm_kernel<<<grid, kThreads, smem, st>>>(p, wmap, amap);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_ex(gemm_kernel, dim3(grid), dim3(kThreads), (size_t)smem, st, pdl, p, wmap, amap);
     if (e != cudaSuccess || p.kspl == 1) return e;
     const long long items = (long long)p.B * (p.N >> 2);
-    gemm_reduce_kernel<<<(unsigned)((items + 255) / 256), 256, 0, st>>>(p);
-    return cudaGetLastError();
+    return launch_ex(gemm_reduce_kernel, dim3((unsigned)((items + 255) / 256)), dim3(256), 0, st, pdl, p);
 }
 
-cudaError_t launch_gemm_split(const float* A, int lda, int K, int B, uint8_t* As, float* unscale, cudaStream_t st) {
-    split_rows_kernel<<<B, 256, 0, st>>>(A, lda, K, As, unscale);
-    return cudaGetLastError();
+cudaError_t launch_gemm_split(const float* A, int lda, int K, int B, uint8_t* As, float* unscale, cudaStream_t st,
+                              bool pdl) {
+    return launch_ex(split_rows_kernel, dim3(B), dim3(256), 0, st, pdl, A, lda, K, As, unscale);
 }
 
 }  // namespace lc

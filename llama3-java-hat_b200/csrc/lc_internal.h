@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <utility>
 #include <cstring>
 #include <vector>
 
@@ -56,7 +57,24 @@ AttnPlan plan_attention(int batch, int n_heads, int n_kv, int head_dim, int max_
 // scratch: attention_scratch_bytes(p) bytes; counters inside are cleared by this call.
 cudaError_t launch_attention_decode(const AttnPlan& p, const float* q, const float* k, const float* v, float* out,
                                     const int32_t* seq_len, int64_t seq_stride, int64_t head_stride,
-                                    int64_t pos_stride, void* scratch, cudaStream_t st);
+                                    int64_t pos_stride, void* scratch, cudaStream_t st, bool pdl = false);
+
+// Launch with optional programmatic stream serialisation.
+template <typename... P, typename... A>
+cudaError_t launch_ex(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                      A&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
+}
 
 // ---- fused decode step (lc_decode.cu) ----
 //
@@ -236,10 +254,13 @@ cudaError_t gemm_prepare();  // sets the shared-memory attribute once
 // the pre-split activations of p.B rows (box: all row groups x 64 columns).
 cudaError_t gemm_make_wmap(CUtensorMap* out, const GemmParams& p);
 cudaError_t gemm_make_amap(CUtensorMap* out, const GemmParams& p);
+// pdl: launched with programmatic stream serialisation (the kernels wait for
+// their predecessor before touching its results; weight loads start early).
 cudaError_t launch_gemm(const GemmParams& p, const CUtensorMap& wmap, const CUtensorMap& amap, int num_sms,
-                        cudaStream_t st);
+                        cudaStream_t st, bool pdl = false);
 // A fp32 [B][lda] -> pre-split activations As and unscale[B].
-cudaError_t launch_gemm_split(const float* A, int lda, int K, int B, uint8_t* As, float* unscale, cudaStream_t st);
+cudaError_t launch_gemm_split(const float* A, int lda, int K, int B, uint8_t* As, float* unscale, cudaStream_t st,
+                              bool pdl = false);
 // Column-block width of the standalone tiled layout: the largest multiple of
 // 64 up to 2048 dividing cols (0: cols % 64 != 0).
 int gemm_tile_width(int cols);

@@ -129,34 +129,52 @@ void launch_rmsnorm_rows(float* x, const float* w, int rows, int width, float ep
 // Thread per (row, head, pair).  freq[] is computed on the host in double
 // exactly like RoPE.java:42; the angle is a float product (RoPE.java:43) and
 // cos/sin are evaluated in double then rounded (RoPE.java:44-45).
-__global__ void rope_rows_kernel(float* __restrict__ vec, const int32_t* __restrict__ pos, int rows, int num_heads,
-                                 int head_dim, RopeFreq fq) {
-    const int half = head_dim >> 1;
-    const long long pairs_per_row = (long long)num_heads * half;
-    const long long total = pairs_per_row * rows;
-    for (long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x; t < total;
-         t += (long long)gridDim.x * blockDim.x) {
-        const int r = (int)(t / pairs_per_row);
-        const int rem = (int)(t % pairs_per_row);
-        const int h = rem / half, j = rem % half;
-        float* v = vec + (size_t)r * num_heads * head_dim + (size_t)h * head_dim + 2 * j;
-        const float val = __fmul_rn((float)pos[r], fq.f[j]);
-        double s, c;
-        sincos((double)val, &s, &c);
-        const float cf = (float)c, sf = (float)s;
-        const float v0 = v[0], v1 = v[1];
-        v[0] = __fsub_rn(__fmul_rn(v0, cf), __fmul_rn(v1, sf));
-        v[1] = __fadd_rn(__fmul_rn(v0, sf), __fmul_rn(v1, cf));
+// One CTA per row at a time.  The angle of pair j depends on (pos, j) only,
+// so its cos / sin (double, rounded to float: RoPE.java:45-46) are computed
+// once per row into shared memory and shared by all heads; the rotation keeps
+// the reference's uncontracted expressions, so results stay bit-identical.
+__global__ void __launch_bounds__(256) rope_rows_kernel(float* __restrict__ vec, const int32_t* __restrict__ pos,
+                                                        int rows, int num_heads, int head_dim, RopeFreq fq) {
+    __shared__ float2 cs[256];  // (cos, sin) per pair index; head_dim <= 512
+    const int half = head_dim >> 1, width = num_heads * head_dim;
+    const bool vec4 = (head_dim % 4 == 0) && ((reinterpret_cast<uintptr_t>(vec) & 15) == 0);
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+        const float p = (float)pos[r];
+        for (int j = threadIdx.x; j < half; j += blockDim.x) {
+            double sd, cd;
+            sincos((double)__fmul_rn(p, fq.f[j]), &sd, &cd);
+            cs[j] = make_float2((float)cd, (float)sd);
+        }
+        __syncthreads();
+        float* v = vec + (size_t)r * width;
+        if (vec4) {
+            for (int q = threadIdx.x; q < width / 4; q += blockDim.x) {
+                float4 x = reinterpret_cast<float4*>(v)[q];
+                const int j = ((4 * q) % head_dim) >> 1;
+                const float2 c0 = cs[j], c1 = cs[j + 1];
+                const float4 o = make_float4(__fsub_rn(__fmul_rn(x.x, c0.x), __fmul_rn(x.y, c0.y)),
+                                             __fadd_rn(__fmul_rn(x.x, c0.y), __fmul_rn(x.y, c0.x)),
+                                             __fsub_rn(__fmul_rn(x.z, c1.x), __fmul_rn(x.w, c1.y)),
+                                             __fadd_rn(__fmul_rn(x.z, c1.y), __fmul_rn(x.w, c1.x)));
+                reinterpret_cast<float4*>(v)[q] = o;
+            }
+        } else {
+            for (int t = threadIdx.x; t < width / 2; t += blockDim.x) {
+                const int j = t % half;
+                const float2 c = cs[j];
+                const float v0 = v[2 * t], v1 = v[2 * t + 1];
+                v[2 * t] = __fsub_rn(__fmul_rn(v0, c.x), __fmul_rn(v1, c.y));
+                v[2 * t + 1] = __fadd_rn(__fmul_rn(v0, c.y), __fmul_rn(v1, c.x));
+            }
+        }
+        __syncthreads();  // cs is rewritten for the next row
     }
 }
 
 void launch_rope_rows(float* vec, const int32_t* pos, int rows, int num_heads, int head_dim, const RopeFreq& fq,
                       cudaStream_t st) {
-    long long total = (long long)rows * num_heads * (head_dim / 2);
-    long long blocks = (total + 255) / 256;
-    if (blocks > 148 * 64) blocks = 148 * 64;
-    if (blocks < 1) blocks = 1;
-    rope_rows_kernel<<<(int)blocks, 256, 0, st>>>(vec, pos, rows, num_heads, head_dim, fq);
+    const int blocks = rows < 148 * 8 ? rows : 148 * 8;
+    rope_rows_kernel<<<blocks < 1 ? 1 : blocks, 256, 0, st>>>(vec, pos, rows, num_heads, head_dim, fq);
 }
 
 // ----------------------------------------------------------- SiLU/SwiGLU --
@@ -202,112 +220,114 @@ void launch_swiglu(float* g, const float* u, long long n, cudaStream_t st) {
 
 // --------------------------------------------------------------- Softmax --
 
-// Online softmax statistics: merge (m, l) pairs, l relative to m.
-LC_DEV void online_merge(float& m, float& l, float m2, float l2) {
-    if (m2 == -INFINITY) return;
-    if (m == -INFINITY) {
-        m = m2;
-        l = l2;
-        return;
+// Softmax.java:28-51 per row: m = max, e_i = exp(x_i - m), sum, inv = 1/sum,
+// x_i = e_i * inv.  exp is the precise float expf (within 2 ulp of the
+// reference's double exp rounded to float) and the sum is a tree, so results
+// match the reference to summation order and those ulps.  The row is read
+// once and written once.
+
+// Rows of up to 32 * EPL floats: one warp per row, EPL floats per lane.
+template <int EPL>
+__global__ void __launch_bounds__(256) softmax_rows_warp_kernel(float* __restrict__ x, int rows, int width) {
+    const int lane = threadIdx.x & 31;
+    const long long r = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    float* row = x + (size_t)r * (size_t)width;
+    float v[EPL];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) {
+        const int i = lane + 32 * k;
+        v[k] = i < width ? row[i] : -INFINITY;
+        m = fmaxf(m, v[k]);
     }
-    if (m2 > m) {
-        l = fmaf(l, exp_via_double(m - m2), l2);
-        m = m2;
-    } else {
-        l = fmaf(l2, exp_via_double(m2 - m), l);
+    m = warp_max(m);
+    float l = 0.0f;
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) {
+        v[k] = (lane + 32 * k < width) ? expf(__fsub_rn(v[k], m)) : 0.0f;
+        l += v[k];
+    }
+    l = warp_sum(l);
+    const float inv = __fdiv_rn(1.0f, l);
+#pragma unroll
+    for (int k = 0; k < EPL; ++k) {
+        const int i = lane + 32 * k;
+        if (i < width) row[i] = __fmul_rn(v[k], inv);
     }
 }
 
-// One CTA per row, the row held in registers: one read pass computes the
-// online (max, sum) statistics, one write pass emits exp(x-max) * (1/sum) --
-// the output values use the exact reference expressions (Softmax.java:41,47-49)
-// with the global max; only the accumulation order of the sum differs.
+// Rows of up to 256 * EPT floats: one CTA per row, EPT floats per thread.
 template <int EPT>
-__global__ void softmax_rows_kernel(float* __restrict__ x, int width) {
-    __shared__ float sm[32], sl[32];
+__global__ void __launch_bounds__(256) softmax_rows_kernel(float* __restrict__ x, int width) {
+    __shared__ float red[8];
     float* row = x + (size_t)blockIdx.x * (size_t)width;
-    float v[EPT];
-    float m = -INFINITY, l = 0.0f;
-#pragma unroll
-    for (int k = 0; k < EPT; ++k) {
-        const int i = threadIdx.x + k * 256;
-        v[k] = (i < width) ? row[i] : -INFINITY;
-        if (i < width) {
-            if (v[k] > m) {
-                l = (m == -INFINITY) ? 0.0f : l * exp_via_double(m - v[k]);
-                m = v[k];
-            }
-            l += exp_via_double(v[k] - m);
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-        float l2 = __shfl_xor_sync(0xffffffffu, l, o);
-        online_merge(m, l, m2, l2);
-    }
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) {
-        sm[w] = m;
-        sl[w] = l;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float M = sm[0], L = sl[0];
-        for (int i = 1; i < 8; ++i) online_merge(M, L, sm[i], sl[i]);
-        sm[0] = M;
-        sl[0] = L;
-    }
-    __syncthreads();
-    const float M = sm[0];
-    const float inv = __fdiv_rn(1.0f, sl[0]);
+    float v[EPT];
+    float m = -INFINITY;
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
         const int i = threadIdx.x + k * 256;
-        if (i < width) row[i] = __fmul_rn(exp_via_double(__fsub_rn(v[k], M)), inv);
+        v[k] = i < width ? row[i] : -INFINITY;
+        m = fmaxf(m, v[k]);
+    }
+    m = warp_max(m);
+    if (lane == 0) red[w] = m;
+    __syncthreads();
+    m = red[0];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) m = fmaxf(m, red[k]);
+    float l = 0.0f;
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+        v[k] = (threadIdx.x + k * 256 < width) ? expf(__fsub_rn(v[k], m)) : 0.0f;
+        l += v[k];
+    }
+    l = warp_sum(l);
+    __syncthreads();  // red reused
+    if (lane == 0) red[w] = l;
+    __syncthreads();
+    float L = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) L += red[k];
+    const float inv = __fdiv_rn(1.0f, L);
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+        const int i = threadIdx.x + k * 256;
+        if (i < width) row[i] = __fmul_rn(v[k], inv);
     }
 }
 
-// Rows wider than the register budget: same statistics, row re-read.
-__global__ void softmax_rows_wide_kernel(float* __restrict__ x, int width) {
-    __shared__ float sm[32], sl[32];
+// Rows wider than the register budget: max pass, exp-sum pass, write pass.
+__global__ void __launch_bounds__(256) softmax_rows_wide_kernel(float* __restrict__ x, int width) {
+    __shared__ float red[8];
     float* row = x + (size_t)blockIdx.x * (size_t)width;
-    float m = -INFINITY, l = 0.0f;
-    for (int i = threadIdx.x; i < width; i += 256) {
-        const float v = row[i];
-        if (v > m) {
-            l = (m == -INFINITY) ? 0.0f : l * exp_via_double(m - v);
-            m = v;
-        }
-        l += exp_via_double(v - m);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-        float l2 = __shfl_xor_sync(0xffffffffu, l, o);
-        online_merge(m, l, m2, l2);
-    }
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) {
-        sm[w] = m;
-        sl[w] = l;
-    }
+    float m = -INFINITY;
+    for (int i = threadIdx.x; i < width; i += 256) m = fmaxf(m, row[i]);
+    m = warp_max(m);
+    if (lane == 0) red[w] = m;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float M = sm[0], L = sl[0];
-        for (int i = 1; i < 8; ++i) online_merge(M, L, sm[i], sl[i]);
-        sm[0] = M;
-        sl[0] = L;
-    }
+    m = red[0];
+    for (int k = 1; k < 8; ++k) m = fmaxf(m, red[k]);
+    float l = 0.0f;
+    for (int i = threadIdx.x; i < width; i += 256) l += expf(__fsub_rn(row[i], m));
+    l = warp_sum(l);
     __syncthreads();
-    const float M = sm[0];
-    const float inv = __fdiv_rn(1.0f, sl[0]);
-    for (int i = threadIdx.x; i < width; i += 256) row[i] = __fmul_rn(exp_via_double(__fsub_rn(row[i], M)), inv);
+    if (lane == 0) red[w] = l;
+    __syncthreads();
+    float L = 0.0f;
+    for (int k = 0; k < 8; ++k) L += red[k];
+    const float inv = __fdiv_rn(1.0f, L);
+    for (int i = threadIdx.x; i < width; i += 256) row[i] = __fmul_rn(expf(__fsub_rn(row[i], m)), inv);
 }
 
 void launch_softmax_rows(float* x, int rows, int width, cudaStream_t st) {
-    if (width <= 256) softmax_rows_kernel<1><<<rows, 256, 0, st>>>(x, width);
-    else if (width <= 1024) softmax_rows_kernel<4><<<rows, 256, 0, st>>>(x, width);
+    const unsigned wgrid = (unsigned)((rows + 7) / 8);
+    if (width <= 128) softmax_rows_warp_kernel<4><<<wgrid, 256, 0, st>>>(x, rows, width);
+    else if (width <= 256) softmax_rows_warp_kernel<8><<<wgrid, 256, 0, st>>>(x, rows, width);
+    else if (width <= 512) softmax_rows_warp_kernel<16><<<wgrid, 256, 0, st>>>(x, rows, width);
+    else if (width <= 1024) softmax_rows_warp_kernel<32><<<wgrid, 256, 0, st>>>(x, rows, width);
     else if (width <= 4096) softmax_rows_kernel<16><<<rows, 256, 0, st>>>(x, width);
     else if (width <= 8192) softmax_rows_kernel<32><<<rows, 256, 0, st>>>(x, width);
     else softmax_rows_wide_kernel<<<rows, 256, 0, st>>>(x, width);

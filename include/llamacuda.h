@@ -91,9 +91,10 @@ int lc_weights_tile(lc_context* ctx, const uint16_t* W, uint16_t* Wt, int rows, 
  * K/GEMV.java:66-91) for `batch` activation rows at once on the tcgen05
  * tensor cores: Y[b][r] = sum_c W[r][c] * X[b][c].  Wt: device memory from
  * lc_weights_tile; X [batch][cols], Y [batch][rows] fp32, host or device.
- * batch 1..64, rows % 16 == 0, cols % 64 == 0.  Each X row is split into
- * f16 hi + lo parts under a power-of-two row scale (2^-22 relative), the
- * products are exact and accumulate in fp32. */
+ * batch 1..16384 (up to 64 rows the weights stream once; more rows run as
+ * tiles of 64, the prefill product), rows % 16 == 0, cols % 64 == 0.  Each X
+ * row is split into f16 hi + lo parts under a power-of-two row scale (2^-22
+ * relative), the products are exact and accumulate in fp32. */
 int lc_gemm_f16_tiled(lc_context* ctx, const uint16_t* Wt, const float* X, float* Y, int rows, int cols, int batch);
 
 /* lc_gemm_f16_tiled as a logits slice with its argmax: Y (may be NULL) as

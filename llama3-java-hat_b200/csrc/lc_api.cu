@@ -318,9 +318,9 @@ extern "C" int lc_weights_tile(lc_context* c, const uint16_t* W, uint16_t* Wt, i
 static int gemm_tiled(lc_context* c, const uint16_t* Wt, const float* X, float* Y, int rows, int cols, int batch,
                       int idx_offset, uint64_t* keys) {
     CTX_CHECK(c);
-    if (rows <= 0 || cols <= 0 || batch <= 0 || batch > kGemmMaxB || rows % 16 || gemm_tile_width(cols) == 0)
+    if (rows <= 0 || cols <= 0 || batch <= 0 || batch > kGemmMaxRows || rows % 16 || gemm_tile_width(cols) == 0)
         return fail(LC_ERR_INVALID_ARG, "rows=%d cols=%d batch=%d (rows %% 16 == 0, cols %% 64 == 0, batch 1..%d)",
-                    rows, cols, batch, kGemmMaxB);
+                    rows, cols, batch, kGemmMaxRows);
     GemmParams g;
     memset(&g, 0, sizeof(g));
     g.N = rows;
@@ -335,7 +335,7 @@ static int gemm_tiled(lc_context* c, const uint16_t* Wt, const float* X, float* 
     auto* dK = keys ? (unsigned long long*)s.arg(keys, (size_t)batch * 8, kOut) : nullptr;
     if (s.status != LC_OK) return s.status;
     if (((uintptr_t)dW | (uintptr_t)dX | (uintptr_t)dY) & 15) return fail(LC_ERR_INVALID_ARG, "buffers must be 16-byte aligned");
-    const size_t off_a = 256;
+    const size_t off_a = ((size_t)batch * 4 + 255) / 256 * 256;  // row scales first
     const size_t off_p = off_a + ((gemm_split_bytes(batch, cols) + 255) / 256) * 256;
     const size_t need = off_p + gemm_part_bytes(g);
     if (c->gemm_scratch_bytes < need) {

@@ -104,7 +104,8 @@ __device__ __forceinline__ unsigned long long apply4(const GemmParams& p, int s,
                 const bool isk = n < p.qdim + p.kvd;
                 const int rr = n - p.qdim - (isk ? 0 : p.kvd);
                 float* base = isk ? p.kcache : p.vcache;
-                float* dst = base + (size_t)s * p.kv_seq_stride + (size_t)(rr / kGemmHeadDim) * p.kv_head_stride +
+                const int seq = p.row_seq ? p.row_seq[s] : s;
+                float* dst = base + (size_t)seq * p.kv_seq_stride + (size_t)(rr / kGemmHeadDim) * p.kv_head_stride +
                              (size_t)pos * kGemmHeadDim + (rr & (kGemmHeadDim - 1));
                 *reinterpret_cast<float4*>(dst) = v;
             }
@@ -135,6 +136,17 @@ __device__ __forceinline__ unsigned long long apply4(const GemmParams& p, int s,
     return 0ull;
 }
 
+// Unit u -> (K split, row tile, N block): the split varies fastest, then the
+// row tile, so consecutive CTAs share an N block of weights (L2 reuse when
+// there are several row tiles).
+struct Unit {
+    int ks, mt, nbi;
+};
+__device__ __forceinline__ Unit unit_of(const GemmParams& p, int u) {
+    const int rest = u / p.kspl;
+    return Unit{u % p.kspl, rest % p.mtiles, rest / p.mtiles};
+}
+
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ GemmParams p,
                                                            const __grid_constant__ CUtensorMap wmap,
                                                            const __grid_constant__ CUtensorMap amap) {
@@ -142,7 +154,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const int NS = p.stages, SB = p.stage_bytes;
     Bars* bs = reinterpret_cast<Bars*>(smem + NS * SB);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, G = gridDim.x;
-    const int krange = p.K / p.kspl, nchunk = krange / kKC, nrg = (p.B + 3) >> 2;
+    const int krange = p.K / p.kspl, nchunk = krange / kKC;
+    const int nrg = p.mtiles > 1 ? 16 : (p.B + 3) >> 2;  // activation row groups per box
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -175,8 +188,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             // results the activation boxes carry).
             const int u0 = blockIdx.x;
             const int pre = u0 < p.units ? min(NS, nchunk) : 0;
+            const Unit U0 = unit_of(p, u0);
             {
-                const int ks = u0 % p.kspl, g0 = ((u0 / p.kspl) * p.nblk) >> 3;
+                const int ks = U0.ks, g0 = (U0.nbi * p.nblk) >> 3;
                 for (int c = 0; c < pre; ++c) {
                     const int kc = ks * krange + c * kKC;
                     mbar_arrive_expect_tx(&bs->full[c], tx);
@@ -186,11 +200,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             }
             griddep_wait();
             for (int c = 0; c < pre; ++c)
-                tma_load_3d(smem + c * SB, &amap, 0, ((u0 % p.kspl) * krange + c * kKC) >> 3, 0, &bs->full[c], apol);
+                tma_load_3d(smem + c * SB, &amap, 0, (U0.ks * krange + c * kKC) >> 3, U0.mt * 16, &bs->full[c], apol);
             uint32_t it = (uint32_t)pre, slot = (uint32_t)(pre % NS), par = pre == NS ? 0u : 1u;
             bool ok = true;
             for (int u = blockIdx.x; u < p.units && ok; u += G) {
-                const int ks = u % p.kspl, g0 = ((u / p.kspl) * p.nblk) >> 3;
+                const Unit U = unit_of(p, u);
+                const int ks = U.ks, g0 = (U.nbi * p.nblk) >> 3;
                 for (int c = (u == u0 ? pre : 0); c < nchunk; ++c) {
                     if (!mbar_wait_bounded(&bs->empty[slot], par, p.err, globaltimer_ns() + p.timeout_ns,
                                            kDevTimeoutEmpty)) {
@@ -201,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     uint8_t* st = smem + slot * SB;
                     mbar_arrive_expect_tx(&bs->full[slot], tx);
                     tma_load_4d(st + kABytes, &wmap, 0, (kc % p.cbw) >> 3, kc / p.cbw, g0, &bs->full[slot], wpol);
-                    tma_load_3d(st, &amap, 0, kc >> 3, 0, &bs->full[slot], apol);
+                    tma_load_3d(st, &amap, 0, kc >> 3, U.mt * 16, &bs->full[slot], apol);
                     ++it;
                     if (++slot == (uint32_t)NS) {
                         slot = 0;
@@ -222,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             int j = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < p.units && ok; u += G, ++j) {
-                const int a = j & 1, n0 = (u / p.kspl) * p.nblk, nb = min(p.nblk, p.N - n0);
+                const int a = j & 1, n0 = unit_of(p, u).nbi * p.nblk, nb = min(p.nblk, p.N - n0);
                 if (!mbar_wait_bounded(&bs->dempty[a], ((j >> 1) & 1) ^ 1, p.err, globaltimer_ns() + p.timeout_ns,
                                        kDevTimeoutFull)) {
                     ok = false;
@@ -258,15 +273,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     } else {
         // -------------------------------------------------------- epilogue --
         griddep_wait();  // unscale and the epilogue's outputs belong to the predecessor's stream order
-        const int et = threadIdx.x - kEpiT0, q4 = warp & 3, r = q4 * 32 + lane, s = r >> 1;
-        const bool lead = (r & 1) == 0 && s < p.B;
-        const float unscale = s < p.B ? __ldcg(p.unscale + s) : 0.0f;
+        const int et = threadIdx.x - kEpiT0, q4 = warp & 3, r = q4 * 32 + lane, sl = r >> 1;
         int j = 0;
         for (int u = blockIdx.x; u < p.units; u += G, ++j) {
             // Dependents may launch once every CTA is in its last epilogue
             // (earlier, their blocks would compete with the weight stream).
             if (u + G >= p.units) griddep_launch();
-            const int a = j & 1, nbi = u / p.kspl, ks = u % p.kspl, n0 = nbi * p.nblk, nb = min(p.nblk, p.N - n0);
+            const Unit U = unit_of(p, u);
+            const int a = j & 1, ks = U.ks, n0 = U.nbi * p.nblk, nb = min(p.nblk, p.N - n0);
+            const int s = U.mt * kGemmMaxB + sl;  // activation row of this lane pair
+            const bool lead = (r & 1) == 0 && s < p.B;
+            const float unscale = s < p.B ? __ldcg(p.unscale + s) : 0.0f;
             if (et < kGemmMaxB) bs->best[et] = 0ull;
             bool got = mbar_wait_bounded(&bs->dfull[a], (j >> 1) & 1, p.err, globaltimer_ns() + p.timeout_ns,
                                          kDevTimeoutFull);
@@ -289,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         for (int qd = 0; qd < 4; ++qd) {
                             float y4[4] = {y[4 * qd], y[4 * qd + 1], y[4 * qd + 2], y[4 * qd + 3]};
                             const unsigned long long k = apply4(p, s, n0 + c0 + 4 * qd, y4);
-                            if (k) atomicMax(&bs->best[s], k);
+                            if (k) atomicMax(&bs->best[sl], k);
                         }
                     } else {
                         float4* dst = reinterpret_cast<float4*>(p.part + ((size_t)ks * p.B + s) * p.N + n0 + c0);
@@ -303,7 +320,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             named_bar_sync(kBarEpi, 128);
             if (et == 0) mbar_arrive(&bs->dempty[a]);
             named_bar_sync(kBarEpi, 128);
-            if (et < p.B && p.op == kGemmLogits && bs->best[et]) atomicMax(p.best + et, bs->best[et]);
+            if (et < kGemmMaxB && U.mt * kGemmMaxB + et < p.B && p.op == kGemmLogits && bs->best[et])
+                atomicMax(p.best + U.mt * kGemmMaxB + et, bs->best[et]);
             named_bar_sync(kBarEpi, 128);
         }
     }
@@ -395,10 +413,22 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
 }  // namespace
 
 bool gemm_plan(GemmParams* p, int num_sms) {
-    if (p->B < 1 || p->B > kGemmMaxB || p->N < 16 || p->N % 16 || p->K < kKC || p->K % kKC || p->cbw < kKC ||
-        p->cbw % kKC || p->K % p->cbw)
+    if (p->B < 1 || p->N < 16 || p->N % 16 || p->K < kKC || p->K % kKC || p->cbw < kKC || p->cbw % kKC ||
+        p->K % p->cbw)
         return false;
-    const int G = num_sms > 0 ? num_sms : 1, nrg = (p->B + 3) / 4;
+    const int G = num_sms > 0 ? num_sms : 1;
+    p->mtiles = (p->B + kGemmMaxB - 1) / kGemmMaxB;
+    if (p->mtiles > 1) {
+        // Many row tiles (prefill): the product is compute- and L2-bound;
+        // widest N blocks, whole K per unit.
+        p->nblk = kMaxN;
+        p->kspl = 1;
+        p->units = p->mtiles * ((p->N + kMaxN - 1) / kMaxN);
+        p->stage_bytes = kABytes + kMaxN * kKC * 2;
+        p->stages = kRingBytes / p->stage_bytes;
+        return true;
+    }
+    const int nrg = (p->B + 3) / 4;
     double best = 1e300;
     for (int nblk = kMaxN; nblk >= 16; nblk -= 16) {
         const int nbk = (p->N + nblk - 1) / nblk;
@@ -480,10 +510,10 @@ cudaError_t gemm_make_wmap(CUtensorMap* out, const GemmParams& p) {
 cudaError_t gemm_make_amap(CUtensorMap* out, const GemmParams& p) {
     auto enc = encode_fn();
     if (!enc || ((uintptr_t)p.As & 15)) return cudaErrorInvalidValue;
-    const int nrg = (p.B + 3) / 4;
+    const int nrg = (p.B + 3) / 4;  // row groups stored; a box past them reads zeros
     cuuint64_t dims[3] = {64, (cuuint64_t)(p.K / 8), (cuuint64_t)nrg};
     cuuint64_t strides[2] = {128, (cuuint64_t)(p.K / 8) * 128};
-    cuuint32_t box[3] = {64, kKC / 8, (cuuint32_t)nrg};
+    cuuint32_t box[3] = {64, kKC / 8, (cuuint32_t)(nrg < 16 ? nrg : 16)};
     cuuint32_t es[3] = {1, 1, 1};
     CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint8_t*>(p.As), dims, strides, box, es,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

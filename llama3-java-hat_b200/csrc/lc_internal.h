@@ -204,7 +204,8 @@ enum GemmOp : int {
     kGemmLogits = 4,  // logits[s][n] (optional) and best[s] = packed (value, lowest index) argmax
 };
 
-constexpr int kGemmMaxB = 64;
+constexpr int kGemmMaxB = 64;        // activation rows per row tile (one MMA of 128 hi / lo rows)
+constexpr int kGemmMaxRows = 16384;  // activation rows of one product call (prefill)
 constexpr int kGemmHeadDim = 64;  // head_dim of the kGemmQKV epilogue
 
 // Bytes of the pre-split activations of B rows and K columns.
@@ -216,8 +217,9 @@ struct GemmParams {
     int rows_mem;     // rows stored in W (multiple of 8, <= N; 0: N)
     const uint8_t* As;      // pre-split activations
     const float* unscale;   // [B]
-    int B;
-    int nblk, kspl, units;  // N-block rows, K splits, (N-blocks) * kspl
+    int B;                  // activation rows; more than 64 run as tiles of 64 rows
+    int nblk, kspl, units;  // N-block rows, K splits, row tiles * N-blocks * kspl
+    int mtiles;             // row tiles of 64
     int stages, stage_bytes;
     float* part;             // [kspl][B][N] partial sums when kspl > 1
     int op;
@@ -230,6 +232,7 @@ struct GemmParams {
     float* vcache;            // this layer's base: + s * kv_seq_stride + head * kv_head_stride + pos * 64
     int64_t kv_seq_stride, kv_head_stride;
     const int32_t* pos;       // [B]
+    const int32_t* row_seq;   // [B] KV-cache sequence of each row (null: the row index)
     const float* rope_freq;   // [head_dim / 2]
     // kGemmSwiGLU
     float* h;
@@ -244,8 +247,9 @@ struct GemmParams {
     uint64_t timeout_ns;
 };
 
-// Chooses nblk, kspl and the ring for a grid of `num_sms` CTAs; fills units.
-// Returns false when the shape is unsupported (N % 16, K % 64, K % cbw, B range).
+// Chooses nblk, kspl and the ring for a grid of `num_sms` CTAs; fills units
+// and mtiles.  Returns false when the shape is unsupported (N % 16, K % 64,
+// K % cbw, B < 1).
 bool gemm_plan(GemmParams* p, int num_sms);
 // Bytes of the partial-sum buffer p needs (0 when kspl == 1).
 size_t gemm_part_bytes(const GemmParams& p);

@@ -43,6 +43,7 @@ def test_weights_tile_layout(gemv):
     (512, 2048, 8), (3072, 2048, 64),                   # k / v, fused qkv
     (2048, 8192, 64),                                   # down projection: split K
     (4112, 2048, 64),                                   # rows not a multiple of the N block
+    (2048, 2048, 1000), (512, 8192, 300),               # many row tiles (prefill products)
 ])
 def test_gemm_parity(gemv, oracle, rows, cols, batch):
     rng = np.random.default_rng(rows * 7 + cols + batch)
@@ -113,7 +114,8 @@ def test_gemm_rejects_bad_shapes(gemv):
     X = np.zeros(64 * 65, f32)
     Y = np.zeros(65 * 64, f32)
     with pytest.raises(IllegalArgumentError):
-        gemv.apply_batched_tiled(W, X, Y, 64, 64, 65)  # batch > 64
+        big = np.zeros(16385 * 64, f32)
+        gemv.apply_batched_tiled(W, big, big.copy(), 64, 64, 16385)  # batch past the row limit
     with pytest.raises(IllegalArgumentError):
         gemv.apply_batched_tiled(W, X, Y, 24, 64, 1)   # rows % 16
     with pytest.raises(IllegalArgumentError):

@@ -30,18 +30,21 @@ constexpr int kNormThreads = 256;
 // (LlamaInference.java:122-140), then RMSNorm(x[s]) * w (RMSNorm.java:35-50:
 // invRms = 1 / sqrt(ss / n + eps), x * invRms * w) split into the GEMM's
 // A operand.  best[s] (when given) is cleared for the lm_head that follows.
+// Row s of the output reads activation row in_rows[s] (in_rows null: s); the
+// embedded token is tok[s * tok_stride + pos[s]] (pos null: + 0).
 __global__ void __launch_bounds__(kNormThreads) norm_split_kernel(
     float* __restrict__ x, int dim, const float* __restrict__ w, float eps, const __half* __restrict__ emb,
-    const int32_t* __restrict__ tok, int tok_stride, const int32_t* __restrict__ pos, uint8_t* __restrict__ As,
-    float* __restrict__ unscale, unsigned long long* __restrict__ best) {
+    const int32_t* __restrict__ tok, int tok_stride, const int32_t* __restrict__ pos,
+    const int32_t* __restrict__ in_rows, uint8_t* __restrict__ As, float* __restrict__ unscale,
+    unsigned long long* __restrict__ best) {
     extern __shared__ float ys[];  // dim floats
     __shared__ float red[kNormThreads / 32];
     griddep_launch();
     griddep_wait();
     const int s = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    float* xs = x + (size_t)s * dim;
+    float* xs = x + (size_t)(in_rows ? in_rows[s] : s) * dim;
     if (emb) {
-        const __half* e = emb + (size_t)tok[(size_t)s * tok_stride + pos[s]] * dim;
+        const __half* e = emb + (size_t)tok[(size_t)s * tok_stride + (pos ? pos[s] : 0)] * dim;
         for (int i = tid; i < dim; i += kNormThreads) xs[i] = __half2float(e[i]);
     }
     float ss = 0.0f;
@@ -100,6 +103,110 @@ __global__ void step_end_kernel(int B, int32_t* __restrict__ pos, int32_t* __res
     seqlen[s] = p + 2;
 }
 
+// Causal attention of a prompt (prefill): CTA = (sequence, kv head, block
+// of kPrefillQBlock query positions).  K rows [0, end of the block) are
+// staged in shared memory with a padded stride (lane j reads row j: no bank
+// conflicts), V rows unpadded; each warp takes (query position, query head)
+// pairs: scores with lanes over key positions, softmax by warp reductions
+// (exp in float), values with lanes over dimensions.  Same arithmetic as the
+// decode units up to float rounding (Attention.java:32-61, Softmax.java:28-51
+// per head, positions 0..t).
+constexpr int kPrefillMaxLen = 256;
+constexpr int kPrefillQBlock = 64;
+constexpr int kKPad = kAttnHeadDim + 1;
+
+// Floats of the padded K rows, rounded up so that V starts 16-byte aligned.
+__host__ __device__ inline size_t prefill_k_floats(int rows) { return ((size_t)rows * kKPad + 3) / 4 * 4; }
+
+__host__ __device__ inline size_t prefill_attn_smem(int rows) {
+    return (prefill_k_floats(rows) + (size_t)rows * kAttnHeadDim + 8 * kAttnHeadDim) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(256) prefill_attention_kernel(const float* __restrict__ q,
+                                                                const float* __restrict__ kcache,
+                                                                const float* __restrict__ vcache,
+                                                                float* __restrict__ att,
+                                                                const int32_t* __restrict__ seq_start, int n_heads,
+                                                                int n_kv, int nqb, int64_t kv_seq_stride,
+                                                                int64_t kv_head_stride, float scale) {
+    constexpr int HD = kAttnHeadDim;
+    extern __shared__ float smf[];
+    griddep_launch();
+    griddep_wait();
+    const int qb = blockIdx.x % nqb, kvh = (blockIdx.x / nqb) % n_kv, s = blockIdx.x / (nqb * n_kv);
+    const int r0 = seq_start[s], P = seq_start[s + 1] - r0;
+    const int t0 = qb * kPrefillQBlock;
+    if (t0 >= P) return;
+    const int t1 = min(P, t0 + kPrefillQBlock);  // queries [t0, t1), keys [0, t1)
+    const int kv_mul = n_heads / n_kv, qdim = n_heads * HD;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* Ks = smf;
+    float* Vs = Ks + prefill_k_floats(t1);  // 16-byte aligned: float4 stores below
+    float* qs = Vs + (size_t)t1 * HD + warp * HD;
+    const float* Kb = kcache + (size_t)s * kv_seq_stride + (size_t)kvh * kv_head_stride;
+    const float* Vb = vcache + (size_t)s * kv_seq_stride + (size_t)kvh * kv_head_stride;
+    for (int i = threadIdx.x; i < t1 * (HD / 4); i += 256) {
+        const int t = i / (HD / 4), c = (i % (HD / 4)) * 4;
+        const float4 kk = __ldcg(reinterpret_cast<const float4*>(Kb + (size_t)t * HD + c));
+        const float4 vv = __ldcg(reinterpret_cast<const float4*>(Vb + (size_t)t * HD + c));
+        float* kd = Ks + t * kKPad + c;
+        kd[0] = kk.x;
+        kd[1] = kk.y;
+        kd[2] = kk.z;
+        kd[3] = kk.w;
+        *reinterpret_cast<float4*>(Vs + t * HD + c) = vv;
+    }
+    __syncthreads();
+    constexpr int MJ = kPrefillMaxLen / 32;
+    for (int pr = warp; pr < (t1 - t0) * kv_mul; pr += 8) {
+        const int t = t0 + pr / kv_mul, h = kvh * kv_mul + pr % kv_mul;
+        const float* qr = q + (size_t)(r0 + t) * qdim + h * HD;
+        qs[2 * lane] = __ldcg(qr + 2 * lane);
+        qs[2 * lane + 1] = __ldcg(qr + 2 * lane + 1);
+        __syncwarp();
+        float sc[MJ];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int m = 0; m < MJ; ++m) {
+            const int j = lane + 32 * m;
+            sc[m] = -INFINITY;
+            if (32 * m <= t && j <= t) {
+                const float* kr = Ks + j * kKPad;
+                float d = 0.0f;
+#pragma unroll 16
+                for (int i = 0; i < HD; ++i) d = fmaf(qs[i], kr[i], d);
+                sc[m] = d * scale;
+                mx = fmaxf(mx, sc[m]);
+            }
+        }
+        mx = warp_max(mx);
+        float l = 0.0f;
+#pragma unroll
+        for (int m = 0; m < MJ; ++m) {
+            const float e = (lane + 32 * m <= t) ? expf(sc[m] - mx) : 0.0f;
+            sc[m] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        float2 o = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int m = 0; m < MJ; ++m) {
+            if (32 * m <= t) {
+                const int jn = min(32, t + 1 - 32 * m);
+                for (int jj = 0; jj < jn; ++jj) {
+                    const float e = __shfl_sync(0xffffffffu, sc[m], jj);
+                    const float2 v = *reinterpret_cast<const float2*>(Vs + (32 * m + jj) * HD + 2 * lane);
+                    o.x = fmaf(e, v.x, o.x);
+                    o.y = fmaf(e, v.y, o.y);
+                }
+            }
+        }
+        const float inv = 1.0f / l;
+        *reinterpret_cast<float2*>(att + (size_t)(r0 + t) * qdim + h * HD + 2 * lane) = make_float2(o.x * inv, o.y * inv);
+        __syncwarp();  // qs reused
+    }
+}
+
 enum { kJobQKV = 0, kJobO = 1, kJobGU = 2, kJobDN = 3 };
 
 }  // namespace
@@ -127,6 +234,14 @@ struct BatchEngine {
     cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
     float total_ms = 0.0f, decode_ms = 0.0f;
     int steps_run = 0;
+    bool used_prefill = false;
+    // prefill: one row per prompt token of a call
+    int pcap = 0;
+    float *px = nullptr, *pq = nullptr, *patt = nullptr, *ph = nullptr, *punscale = nullptr;
+    uint8_t* pAs = nullptr;
+    int32_t *prow = nullptr;  // [4][pcap]: token, position, sequence of each row; then seq_start[n + 1], last row[n]
+    std::vector<CUtensorMap> pwmap;  // weight maps of the prefill products (N blocks of 256 rows)
+    bool pattn_ready = false;
 };
 
 namespace {
@@ -151,8 +266,8 @@ cudaError_t enqueue_step(BatchEngine* e, int B, bool lm) {
     constexpr bool pdl = true;
     auto norm = [&](const float* w, const __half* emb, unsigned long long* best) {
         return launch_ex(norm_split_kernel, dim3(B), dim3(kNormThreads), (size_t)m.dim * 4, e->st, pdl, e->x, m.dim,
-                         w, m.eps, emb, (const int32_t*)e->tok, e->tok_stride, (const int32_t*)e->pos, e->As,
-                         e->unscale, best);
+                         w, m.eps, emb, (const int32_t*)e->tok, e->tok_stride, (const int32_t*)e->pos,
+                         (const int32_t*)nullptr, e->As, e->unscale, best);
     };
     for (int l = 0; l < m.n_layers && ce == cudaSuccess; ++l) {
         const LayerW& L = m.layers[l];
@@ -377,8 +492,9 @@ void batch_destroy(BatchEngine* e) {
     if (e->st) cudaStreamSynchronize(e->st);
     if (e->g_lm) cudaGraphExecDestroy(e->g_lm);
     if (e->g_nolm) cudaGraphExecDestroy(e->g_nolm);
-    void* bufs[] = {e->x, e->q, e->att, e->h, e->logits, e->unscale, e->As, e->kcache, e->vcache, e->rope,
-                    e->best, e->pos, e->seqlen, e->nprompt, e->tok, e->part, e->attn_scratch};
+    void* bufs[] = {e->x,    e->q,      e->att,   e->h,      e->logits,   e->unscale, e->As,  e->kcache,
+                    e->vcache, e->rope, e->best,  e->pos,    e->seqlen,   e->nprompt, e->tok, e->part,
+                    e->attn_scratch, e->px, e->pq, e->patt, e->ph, e->punscale, e->pAs, e->prow};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (e->ev0) cudaEventDestroy(e->ev0);
@@ -389,6 +505,185 @@ void batch_destroy(BatchEngine* e) {
 
 int batch_max(const BatchEngine* e) { return e->max_batch; }
 int batch_tok_stride(const BatchEngine* e) { return e->tok_stride; }
+
+namespace {
+
+// The prompts of a call as one row set: every prompt token is a row of the
+// M-tiled products (the weights are read once per 64 rows instead of once
+// per position), the causal attention runs per (sequence, kv head), and the
+// lm_head runs once, on each sequence's last prompt token.  Leaves every
+// sequence at position len_s with its first generated token in place.
+cudaError_t prefill(BatchEngine* e, int n, const std::vector<int32_t>& tok_host, const std::vector<int32_t>& lens) {
+    const BatchModel& m = e->m;
+    const int qdim = m.n_heads * m.head_dim, kvd = m.n_kv * m.head_dim;
+    const size_t layer_kv = (size_t)m.n_kv * m.max_seq * m.head_dim;
+    int M = 0, maxlen = 0;
+    for (int s = 0; s < n; ++s) {
+        M += lens[s];
+        maxlen = std::max(maxlen, lens[s]);
+    }
+    cudaError_t ce = cudaSuccess;
+    if (M > e->pcap) {
+        void* old[] = {e->px, e->pq, e->patt, e->ph, e->punscale, e->pAs, e->prow};
+        for (void* b : old)
+            if (b) cudaFree(b);
+        e->px = e->pq = e->patt = e->ph = e->punscale = nullptr;
+        e->pAs = nullptr;
+        e->prow = nullptr;
+        e->pcap = 0;
+        const int cap = std::max(M, 1024);
+        if ((ce = dalloc(&e->px, (size_t)cap * m.dim)) != cudaSuccess) return ce;
+        if ((ce = dalloc(&e->pq, (size_t)cap * qdim)) != cudaSuccess) return ce;
+        if ((ce = dalloc(&e->patt, (size_t)cap * qdim)) != cudaSuccess) return ce;
+        if ((ce = dalloc(&e->ph, (size_t)cap * m.hidden)) != cudaSuccess) return ce;
+        if ((ce = dalloc(&e->punscale, (size_t)cap)) != cudaSuccess) return ce;
+        if ((ce = dalloc(&e->pAs, gemm_split_bytes(cap, e->kmax))) != cudaSuccess) return ce;
+        if ((ce = dalloc(&e->prow, (size_t)3 * cap + 2 * kGemmMaxB + 2)) != cudaSuccess) return ce;
+        e->pcap = cap;
+    }
+    // rows: token, position, sequence; then sequence starts and last rows
+    std::vector<int32_t> rows((size_t)3 * e->pcap + 2 * kGemmMaxB + 2, 0);
+    int32_t* rtok = rows.data();
+    int32_t* rpos = rtok + e->pcap;
+    int32_t* rseq = rpos + e->pcap;
+    int32_t* sstart = rseq + e->pcap;
+    int32_t* slast = sstart + kGemmMaxB + 1;
+    std::vector<int32_t> pos_last(n), len1(n);
+    for (int s = 0, r = 0; s < n; ++s) {
+        sstart[s] = r;
+        for (int t = 0; t < lens[s]; ++t, ++r) {
+            rtok[r] = tok_host[(size_t)s * e->tok_stride + t];
+            rpos[r] = t;
+            rseq[r] = s;
+        }
+        slast[s] = r - 1;
+        pos_last[s] = lens[s] - 1;
+        len1[s] = lens[s];
+        sstart[s + 1] = r;
+    }
+    const int32_t* d_tok = e->prow;
+    const int32_t* d_pos = e->prow + e->pcap;
+    const int32_t* d_seq = e->prow + 2 * e->pcap;
+    const int32_t* d_start = e->prow + 3 * e->pcap;
+    const int32_t* d_last = d_start + kGemmMaxB + 1;
+    ce = cudaMemcpyAsync(e->prow, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice, e->st);
+    // the lm_head step below advances position len_s - 1 to len_s
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(e->pos, pos_last.data(), (size_t)n * 4, cudaMemcpyHostToDevice, e->st);
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(e->seqlen, len1.data(), (size_t)n * 4, cudaMemcpyHostToDevice, e->st);
+    if (ce != cudaSuccess) return ce;
+
+    // products of M rows (row tiles of 64, N blocks of 256, whole K per unit)
+    GemmParams base;
+    memset(&base, 0, sizeof(base));
+    base.cbw = m.dim;
+    base.B = M;
+    base.As = e->pAs;
+    base.unscale = e->punscale;
+    base.err = e->err;
+    base.timeout_ns = 2000000000ull;
+    std::vector<GemmParams> gp(4 * m.n_layers, base);
+    for (int j = 0; j < 4 * m.n_layers; ++j) {
+        GemmParams& g = gp[j];
+        const int l = j / 4, kind = j % 4;
+        const LayerW& L = m.layers[l];
+        if (kind == kJobQKV) {
+            g.W = L.wqkv;
+            g.N = qdim + 2 * kvd;
+            g.K = m.dim;
+            g.op = kGemmQKV;
+            g.q = e->pq;
+            g.qdim = qdim;
+            g.kvd = kvd;
+            g.kcache = e->kcache + l * layer_kv;
+            g.vcache = e->vcache + l * layer_kv;
+            g.kv_seq_stride = (int64_t)kv_floats_per_seq(m);
+            g.kv_head_stride = (int64_t)m.max_seq * m.head_dim;
+            g.pos = d_pos;
+            g.row_seq = d_seq;
+            g.rope_freq = e->rope;
+        } else if (kind == kJobO) {
+            g.W = L.wo;
+            g.N = m.dim;
+            g.K = qdim;
+            g.op = kGemmResid;
+            g.y = e->px;
+            g.ldy = m.dim;
+        } else if (kind == kJobGU) {
+            g.W = L.wgu;
+            g.N = 2 * m.hidden;
+            g.K = m.dim;
+            g.op = kGemmSwiGLU;
+            g.h = e->ph;
+            g.ldh = m.hidden;
+        } else {
+            g.W = L.wdown;
+            g.N = m.dim;
+            g.K = m.hidden;
+            g.op = kGemmResid;
+            g.y = e->px;
+            g.ldy = m.dim;
+        }
+        g.rows_mem = g.N;
+        if (!gemm_plan(&g, e->sms) || g.kspl != 1) return cudaErrorInvalidValue;
+    }
+    if (e->pwmap.size() != gp.size()) {
+        e->pwmap.resize(gp.size());
+        for (size_t j = 0; j < gp.size(); ++j)
+            if ((ce = gemm_make_wmap(&e->pwmap[j], gp[j])) != cudaSuccess) return ce;
+    }
+    CUtensorMap a_dim, a_qdim, a_hidden;
+    GemmParams a = base;
+    a.K = m.dim;
+    if ((ce = gemm_make_amap(&a_dim, a)) != cudaSuccess) return ce;
+    a.K = qdim;
+    if ((ce = gemm_make_amap(&a_qdim, a)) != cudaSuccess) return ce;
+    a.K = m.hidden;
+    if ((ce = gemm_make_amap(&a_hidden, a)) != cudaSuccess) return ce;
+    const int nqb = (maxlen + kPrefillQBlock - 1) / kPrefillQBlock;
+    const size_t asmem = prefill_attn_smem(std::min(maxlen, nqb * kPrefillQBlock));
+    if (!e->pattn_ready) {
+        ce = cudaFuncSetAttribute(prefill_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)prefill_attn_smem(kPrefillMaxLen));
+        if (ce != cudaSuccess) return ce;
+        e->pattn_ready = true;
+    }
+    const float scale = 1.0f / (float)sqrt((double)m.head_dim);  // Attention.java:33
+    auto norm = [&](const float* w, const __half* emb) {
+        return launch_ex(norm_split_kernel, dim3(M), dim3(kNormThreads), (size_t)m.dim * 4, e->st, false, e->px,
+                         m.dim, w, m.eps, emb, d_tok, 1, (const int32_t*)nullptr, (const int32_t*)nullptr, e->pAs,
+                         e->punscale, (unsigned long long*)nullptr);
+    };
+    for (int l = 0; l < m.n_layers && ce == cudaSuccess; ++l) {
+        const LayerW& L = m.layers[l];
+        const int j = 4 * l;
+        ce = norm(L.attn_norm, l == 0 ? m.tok_emb : nullptr);
+        if (ce == cudaSuccess) ce = launch_gemm(gp[j + kJobQKV], e->pwmap[j + kJobQKV], a_dim, e->sms, e->st);
+        if (ce == cudaSuccess)
+            ce = launch_ex(prefill_attention_kernel, dim3((unsigned)(n * m.n_kv * nqb)), dim3(256), asmem, e->st,
+                           false, (const float*)e->pq, (const float*)(e->kcache + l * layer_kv),
+                           (const float*)(e->vcache + l * layer_kv), e->patt, d_start, m.n_heads, m.n_kv, nqb,
+                           (int64_t)kv_floats_per_seq(m), (int64_t)m.max_seq * m.head_dim, scale);
+        if (ce == cudaSuccess) ce = launch_gemm_split(e->patt, qdim, qdim, M, e->pAs, e->punscale, e->st);
+        if (ce == cudaSuccess) ce = launch_gemm(gp[j + kJobO], e->pwmap[j + kJobO], a_qdim, e->sms, e->st);
+        if (ce == cudaSuccess) ce = norm(L.ffn_norm, nullptr);
+        if (ce == cudaSuccess) ce = launch_gemm(gp[j + kJobGU], e->pwmap[j + kJobGU], a_dim, e->sms, e->st);
+        if (ce == cudaSuccess) ce = launch_gemm_split(e->ph, m.hidden, m.hidden, M, e->pAs, e->punscale, e->st);
+        if (ce == cudaSuccess) ce = launch_gemm(gp[j + kJobDN], e->pwmap[j + kJobDN], a_hidden, e->sms, e->st);
+    }
+    if (ce != cudaSuccess) return ce;
+    // lm_head on the last prompt token of each sequence, then its first token
+    const int jl = 4 * m.n_layers;
+    ce = launch_ex(norm_split_kernel, dim3(n), dim3(kNormThreads), (size_t)m.dim * 4, e->st, false, e->px, m.dim,
+                   m.out_norm, m.eps, (const __half*)nullptr, (const int32_t*)nullptr, 0, (const int32_t*)nullptr,
+                   d_last, e->As, e->unscale, e->best);
+    if (ce == cudaSuccess) ce = launch_gemm(e->gp[jl], e->wmap[jl], e->amap_dim, e->sms, e->st);
+    if (ce == cudaSuccess)
+        ce = launch_ex(step_end_kernel, dim3(1), dim3(kGemmMaxB), 0, e->st, false, n, e->pos, e->seqlen, e->tok,
+                       e->tok_stride, (const int32_t*)e->nprompt, (const unsigned long long*)e->best, 1);
+    return ce;
+}
+
+}  // namespace
 
 cudaError_t batch_run(BatchEngine* e, int n, const std::vector<int32_t>& tok_host, const std::vector<int32_t>& lens,
                       int max_new, std::vector<int32_t>* tok_out) {
@@ -401,16 +696,29 @@ cudaError_t batch_run(BatchEngine* e, int n, const std::vector<int32_t>& tok_hos
     if (ce == cudaSuccess) ce = cudaMemcpyAsync(e->seqlen, ones.data(), (size_t)n * 4, cudaMemcpyHostToDevice, e->st);
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->st);  // host vectors go out of scope
     if (ce != cudaSuccess) return ce;
-    int steps = 0, first_lm = 1 << 30, p_dec = 0;
+    int steps = 0, first_lm = 1 << 30, p_dec = 0, M = 0, maxlen = 0;
     for (int s = 0; s < n; ++s) {
         steps = std::max(steps, lens[s] + max_new - 1);
         first_lm = std::min(first_lm, lens[s] - 1);
         p_dec = std::max(p_dec, lens[s] - 1);
+        M += lens[s];
+        maxlen = std::max(maxlen, lens[s]);
     }
+    // Prompts of more than one row tile (64 tokens) in all, up to
+    // kPrefillMaxLen tokens each and kGemmMaxRows in all, run as one prefill;
+    // otherwise prompt positions step one at a time.
+    e->used_prefill = M > kGemmMaxB && maxlen <= kPrefillMaxLen && M <= kGemmMaxRows;
     ce = cudaEventRecord(e->ev0, e->st);
-    for (int p = 0; p < steps && ce == cudaSuccess; ++p) {
-        if (p == p_dec) ce = cudaEventRecord(e->ev1, e->st);
-        if (ce == cudaSuccess) ce = cudaGraphLaunch(p >= first_lm ? e->g_lm : e->g_nolm, e->st);
+    if (e->used_prefill) {
+        if (ce == cudaSuccess) ce = prefill(e, n, tok_host, lens);
+        if (ce == cudaSuccess) ce = cudaEventRecord(e->ev1, e->st);
+        for (int k = 0; k + 1 < max_new && ce == cudaSuccess; ++k) ce = cudaGraphLaunch(e->g_lm, e->st);
+    } else {
+        // the first token comes from position p_dec; the decode phase follows it
+        for (int p = 0; p < steps && ce == cudaSuccess; ++p) {
+            if (ce == cudaSuccess) ce = cudaGraphLaunch(p >= first_lm ? e->g_lm : e->g_nolm, e->st);
+            if (p == p_dec && ce == cudaSuccess) ce = cudaEventRecord(e->ev1, e->st);
+        }
     }
     if (ce == cudaSuccess) ce = cudaEventRecord(e->ev2, e->st);
     if (ce == cudaSuccess) ce = cudaStreamSynchronize(e->st);

@@ -58,6 +58,44 @@ def test_batch_matches_oracle_tiny(tiny, oracle):
             assert np.abs(b.logits(s) - r).max() <= LOGITS_ABS_TOL
 
 
+def test_batch_prefill_matches_oracle_tiny(tiny, oracle):
+    """Prompts of more than 64 tokens in all run as one prefill (row-tiled
+    tcgen05 products, causal prefill attention); the sequences still follow
+    the oracle, with logits within tolerance."""
+    from llamahat import Batch
+    cfg, w, model = tiny
+    om = oracle.OracleModel(cfg, w)
+    rng = np.random.default_rng(17)
+    lens = [20, 3, 64, 1, 37, 9, 70, 12]  # 216 prompt tokens, one longer than a query block
+    prompts = [rng.integers(0, cfg.vocab, n).astype(np.int32) for n in lens]
+    b = Batch(model, 8)
+    outs = b.generate(prompts, 6, stop=())
+    checked = 0
+    for p, g in zip(prompts, outs):
+        assert len(g) == 6
+        checked += follow_oracle(om, p, g, 6)
+    assert checked >= 30
+    for s, (p, g) in enumerate(zip(prompts, outs)):
+        for pos, t in enumerate(list(p) + list(g[:-1])):
+            r = om.forward(int(t), pos)
+        assert np.abs(b.logits(s) - r).max() <= LOGITS_ABS_TOL
+
+
+def test_batch_prefill_agrees_with_stepwise(tiny):
+    """The same prompts through the prefill path (more than 64 tokens in
+    all) and position by position (one sequence at a time) give the same
+    greedy tokens."""
+    from llamahat import Batch
+    cfg, w, model = tiny
+    rng = np.random.default_rng(23)
+    prompts = [rng.integers(0, cfg.vocab, 40).astype(np.int32) for _ in range(4)]
+    b = Batch(model, 4)
+    together = b.generate(prompts, 8, stop=())   # 160 rows: prefill
+    for p, g in zip(prompts, together):
+        alone = b.generate([p], 8, stop=())[0]   # 40 rows: position by position
+        assert list(g) == list(alone)
+
+
 def test_batch_agrees_with_single_sequence_path(tiny):
     """The batch engine (tcgen05 products) and the fused single-sequence
     kernel give the same greedy tokens on the same prompts."""

@@ -518,6 +518,36 @@ def run_kernels(args):
         del Ws
         torch.cuda.empty_cache()
 
+    # Prefill products: 8192 activation rows (64 sequences x 128 prompt
+    # tokens) on the layer shapes; tensor-bound, reported as TFLOP/s of the
+    # useful product (2 M N K) and of the tensor work (the hi / lo halves
+    # double it) against the measured bf16 GEMM peak.
+    tpeak = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tpeak = float(json.load(f)["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        tpeak = 1590.0
+    for rows, cols, name in [(3072, 2048, "fused qkv"), (2048, 2048, "o"), (16384, 2048, "fused gate|up"),
+                             (2048, 8192, "down")]:
+        M = 8192
+        W = (torch.randn(rows * cols, device="cuda") * 0.02).half()
+        Wt = torch.empty(rows * cols, dtype=torch.int16, device="cuda")
+        gemv.tile(W.view(torch.int16), Wt, rows, cols)
+        X = torch.randn(M, cols, device="cuda")
+        Y = torch.empty(M, rows, device="cuda")
+        us = device_us([lambda: gemv.apply_batched_tiled(Wt, X, Y, rows, cols, M)] * 4, st)
+        useful = 2.0 * M * rows * cols / (us * 1e-6) / 1e12
+        d = {"suite": "gemm_tcgen05_prefill", "case": f"{name} {rows}x{cols} rows {M}", "us_per_call": us,
+             "useful_TFLOP_s": useful, "tensor_TFLOP_s": 2 * useful, "frac_of_bf16_peak": 2 * useful / tpeak,
+             "peak_source": "MEASURED_PEAKS.json bf16_tflops (burst)",
+             "algorithmic_bytes": rows * cols * 2 + M * (rows + cols) * 4, "GB_s": (rows * cols * 2 + M * (rows + cols) * 4) / (us * 1e-6) / 1e9,
+             "frac_of_hbm_peak": (rows * cols * 2 + M * (rows + cols) * 4) / (us * 1e-6) / 1e9 / peak}
+        out.append(d)
+        print(json.dumps(d), flush=True)
+        del W, Wt, X, Y
+        torch.cuda.empty_cache()
+
     # Elementwise rows (fp32 ~N(0,1)); copies rotated past 4x L2 where small.
     wn = torch.ones(2048, device="cuda")
     for rows in (1, 64, 4096):

@@ -255,6 +255,20 @@ int lc_forward(lc_session* s, int32_t token, int32_t pos, float* logits, int32_t
 int lc_generate(lc_session* s, const int32_t* prompt, int32_t n_prompt, int32_t max_new, const int32_t* stop,
                 int32_t n_stop, int32_t* out_tokens, int32_t* n_out);
 
+/* Receives generated token number `index` (0-based) while the launch runs. */
+typedef void (*lc_token_callback)(int32_t token, int32_t index, void* user);
+
+/* lc_generate with streaming: the same single launch, but the kernel also
+ * publishes each greedy token to mapped host memory as soon as it is chosen,
+ * and the calling thread invokes on_token(token, index, user) for each one in
+ * order while the launch is still running (the streaming callbacks of the
+ * chat path around LlamaInference.chat, H/LlamaInference.java:227-247).
+ * Every generated id, the stop token included, is passed exactly once before
+ * the call returns; out_tokens / n_out are filled as by lc_generate. */
+int lc_generate_stream(lc_session* s, const int32_t* prompt, int32_t n_prompt, int32_t max_new,
+                       const int32_t* stop, int32_t n_stop, lc_token_callback on_token, void* user,
+                       int32_t* out_tokens, int32_t* n_out);
+
 /* Continues a sequence already holding positions 0..start_pos-1: feeds
  * `token` at start_pos and decodes n_steps greedy steps (positions
  * start_pos..start_pos+n_steps-1), writing the n_steps produced tokens to

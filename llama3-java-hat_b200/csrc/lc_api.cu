@@ -11,7 +11,10 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
+#include <chrono>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/llamacuda.h"
@@ -892,6 +895,9 @@ static void fill_model_params(const lc_model* m, DecodeParams* p) {
     p->sched_stride = m->sched_stride;
     p->wbase = (const uint8_t*)m->arena;
     p->l2_prefetch_tiles = m->l2_prefetch_tiles;
+    p->trace = nullptr;
+    p->trace_words = 0;
+    p->stream = nullptr;
 }
 
 extern "C" int lc_model_finalize(lc_model* m) {
@@ -955,6 +961,8 @@ struct lc_session {
     int32_t* tokens;
     int attn_max_splits = 0;
     int32_t* pinned = nullptr;  // host staging for small transfers
+    int32_t* stream_host = nullptr;  // mapped token stream: [0] = count, [1 + i] = token i
+    int32_t* stream_dev = nullptr;   // its device address
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.0f;
     unsigned long long* trace = nullptr;  // phase trace buffer (debug), grid x trace_words
@@ -1022,6 +1030,8 @@ extern "C" int lc_session_create(lc_model* m, lc_session** out) {
     s->tokens = (int32_t*)ptr[14];
     e = cudaMemset(s->mem, 0, total);
     if (e == cudaSuccess) e = cudaMallocHost((void**)&s->pinned, (size_t)(c.max_seq + 8) * 4);
+    if (e == cudaSuccess) e = cudaHostAlloc((void**)&s->stream_host, (size_t)(c.max_seq + 2) * 4, cudaHostAllocMapped);
+    if (e == cudaSuccess) e = cudaHostGetDevicePointer((void**)&s->stream_dev, s->stream_host, 0);
     if (e == cudaSuccess) e = cudaEventCreate(&s->ev0);
     if (e == cudaSuccess) e = cudaEventCreate(&s->ev1);
     if (e != cudaSuccess) {
@@ -1038,6 +1048,7 @@ extern "C" int lc_session_destroy(lc_session* s) {
     cudaStreamSynchronize(s->m->ctx->stream);
     if (s->mem) cudaFree(s->mem);
     if (s->pinned) cudaFreeHost(s->pinned);
+    if (s->stream_host) cudaFreeHost(s->stream_host);
     if (s->ev0) cudaEventDestroy(s->ev0);
     if (s->ev1) cudaEventDestroy(s->ev1);
     if (s->trace) cudaFree(s->trace);
@@ -1045,9 +1056,17 @@ extern "C" int lc_session_destroy(lc_session* s) {
     return LC_OK;
 }
 
-// Launches the fused kernel for positions pos0..pos0+nsteps-1 and waits.
+// Host end of the token stream: the callback and its argument.
+struct TokenSink {
+    lc_token_callback cb;
+    void* user;
+};
+
+// Launches the fused kernel for positions pos0..pos0+nsteps-1 and waits.  With
+// a sink, the kernel publishes each generated token to the session's mapped
+// stream buffer and this thread hands them to the callback while it waits.
 static int run_steps(lc_session* s, int pos0, int nsteps, int n_prompt, int skip_prefill_logits,
-                     const int32_t* stop, int n_stop, int* n_done) {
+                     const int32_t* stop, int n_stop, int* n_done, const TokenSink* sink = nullptr) {
     lc_model* m = s->m;
     cudaStream_t st = m->ctx->stream;
     DecodeParams p;
@@ -1088,6 +1107,10 @@ static int run_steps(lc_session* s, int pos0, int nsteps, int n_prompt, int skip
     p.attn_max_splits = s->attn_max_splits;
     p.trace = s->trace;
     p.trace_words = s->trace_words;
+    if (sink) {
+        s->stream_host[0] = 0;  // host memory: written before the launch is enqueued
+        p.stream = s->stream_dev;
+    }
     if (s->trace)
         CK(cudaMemsetAsync(s->trace, 0, (size_t)m->launch.grid * s->trace_words * 8, st), "clear trace");
     CK(cudaMemsetAsync(s->err, 0, sizeof(int), st), "clear error word");
@@ -1096,6 +1119,23 @@ static int run_steps(lc_session* s, int pos0, int nsteps, int n_prompt, int skip
     CK(cudaEventRecord(s->ev1, st), "event");
     CK(cudaMemcpyAsync(s->pinned, s->err, 4, cudaMemcpyDeviceToHost, st), "read error word");
     CK(cudaMemcpyAsync(s->pinned + 1, s->n_done, 4, cudaMemcpyDeviceToHost, st), "read step count");
+    if (sink) {
+        // Poll the published count; after the stream reports completion one
+        // more pass delivers what the last check had not seen.
+        const volatile int32_t* hs = s->stream_host;
+        const int limit = m->cfg.max_seq;
+        int delivered = 0;
+        for (;;) {
+            const cudaError_t q = cudaStreamQuery(st);
+            if (q != cudaSuccess && q != cudaErrorNotReady) CK(q, "decode kernel");
+            int avail = hs[0];
+            std::atomic_thread_fence(std::memory_order_acquire);
+            if (avail > limit) avail = limit;
+            for (; delivered < avail; ++delivered) sink->cb(hs[1 + delivered], delivered, sink->user);
+            if (q == cudaSuccess) break;
+            std::this_thread::sleep_for(std::chrono::microseconds(20));
+        }
+    }
     CK(cudaStreamSynchronize(st), "decode kernel");
     cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1);
     const int err = s->pinned[0];
@@ -1125,8 +1165,8 @@ extern "C" int lc_forward(lc_session* s, int32_t token, int32_t pos, float* logi
     return LC_OK;
 }
 
-extern "C" int lc_generate(lc_session* s, const int32_t* prompt, int32_t n_prompt, int32_t max_new,
-                           const int32_t* stop, int32_t n_stop, int32_t* out_tokens, int32_t* n_out) {
+static int generate_impl(lc_session* s, const int32_t* prompt, int32_t n_prompt, int32_t max_new, const int32_t* stop,
+                         int32_t n_stop, int32_t* out_tokens, int32_t* n_out, const TokenSink* sink) {
     if (!s || !prompt || !out_tokens || !n_out) return fail(LC_ERR_INVALID_ARG, "NULL argument");
     CTX_CHECK(s->m->ctx);
     const lc_config& c = s->m->cfg;
@@ -1141,7 +1181,7 @@ extern "C" int lc_generate(lc_session* s, const int32_t* prompt, int32_t n_promp
     if (n_stop) CK(cudaMemcpy(hstop, stop, (size_t)n_stop * 4, cudaMemcpyDefault), "stop tokens");
     CK(cudaMemcpyAsync(s->tokens, prompt, (size_t)n_prompt * 4, cudaMemcpyDefault, st), "prompt upload");
     int done = 0;
-    int rc = run_steps(s, 0, n_prompt + max_new - 1, n_prompt, 1, hstop, n_stop, &done);
+    int rc = run_steps(s, 0, n_prompt + max_new - 1, n_prompt, 1, hstop, n_stop, &done, sink);
     if (rc) return rc;
     const int n_gen = done - (n_prompt - 1);
     if (n_gen > 0)
@@ -1149,6 +1189,19 @@ extern "C" int lc_generate(lc_session* s, const int32_t* prompt, int32_t n_promp
     CK(cudaStreamSynchronize(st), "generate");
     *n_out = n_gen > 0 ? n_gen : 0;
     return LC_OK;
+}
+
+extern "C" int lc_generate(lc_session* s, const int32_t* prompt, int32_t n_prompt, int32_t max_new,
+                           const int32_t* stop, int32_t n_stop, int32_t* out_tokens, int32_t* n_out) {
+    return generate_impl(s, prompt, n_prompt, max_new, stop, n_stop, out_tokens, n_out, nullptr);
+}
+
+extern "C" int lc_generate_stream(lc_session* s, const int32_t* prompt, int32_t n_prompt, int32_t max_new,
+                                  const int32_t* stop, int32_t n_stop, lc_token_callback on_token, void* user,
+                                  int32_t* out_tokens, int32_t* n_out) {
+    if (!on_token) return fail(LC_ERR_INVALID_ARG, "NULL callback");
+    const TokenSink sink{on_token, user};
+    return generate_impl(s, prompt, n_prompt, max_new, stop, n_stop, out_tokens, n_out, &sink);
 }
 
 extern "C" int lc_decode(lc_session* s, int32_t token, int32_t start_pos, int32_t n_steps, int32_t* out_tokens) {

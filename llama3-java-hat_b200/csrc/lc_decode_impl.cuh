@@ -1309,7 +1309,16 @@ __device__ __forceinline__ void run_consumer(const DecodeParams& p, const Smem& 
         }
         bool stop_now = false;
         if (lm_needed(p, pos) && pos + 1 >= p.n_prompt) {
-            if (cta == 0 && tid == 0) p.tokens[pos + 1] = next;
+            if (cta == 0 && tid == 0) {
+                p.tokens[pos + 1] = next;
+                if (p.stream) {
+                    volatile int32_t* hs = p.stream;
+                    const int i = pos + 1 - p.n_prompt;
+                    hs[1 + i] = next;
+                    __threadfence_system();
+                    hs[0] = i + 1;
+                }
+            }
             for (int k = 0; k < p.n_stop; ++k) stop_now |= (p.stop[k] == next);
         }
         if (ok) steps_done = s + 1;

@@ -149,6 +149,10 @@ struct DecodeParams {
     // %globaltimer stamps into trace[cta*trace_words + k].
     unsigned long long* trace;
     int trace_words;
+    // Token stream (nullable; mapped host memory): CTA 0 writes generated
+    // token i to stream[1 + i], then i + 1 to stream[0], with a system fence
+    // between, so a host thread can poll the count while the launch runs.
+    int32_t* stream;
     // Producer tile schedule of one position (decode_build_schedule): row
     // cta * sched_stride of `sched` lists the CTA's weight tiles in consumption
     // order as offsets from wbase in 256-byte units, the QKV..DN jobs of all

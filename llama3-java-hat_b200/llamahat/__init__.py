@@ -10,11 +10,12 @@ from .kernels import (Accelerator, CudaAttention, CudaGEMV, CudaKernelFactory, C
                       CudaSoftmax, IAttention, IGEMV, IKernelFactory, IRMSNorm, IRoPE, ISiLU, ISoftmax,
                       default_accelerator)
 from .inference import EOS_TOKEN, Batch, CudaModel, LlamaInference, Session
+from .tokenizer import ChatFormat, Message, Role, StreamDecoder, Tokenizer
 
 __all__ = [
-    "Accelerator", "Batch", "CudaAttention", "CudaGEMV", "CudaKernelFactory", "CudaModel", "CudaRMSNorm", "CudaRoPE",
-    "CudaSiLU", "CudaSoftmax", "DeviceTimeoutError", "EOS_TOKEN", "IAttention", "IGEMV", "IKernelFactory",
+    "Accelerator", "Batch", "ChatFormat", "CudaAttention", "CudaGEMV", "CudaKernelFactory", "CudaModel",
+    "CudaRMSNorm", "CudaRoPE", "CudaSiLU", "CudaSoftmax", "DeviceTimeoutError", "EOS_TOKEN", "IAttention", "IGEMV", "IKernelFactory",
     "IRMSNorm", "IRoPE", "ISiLU", "ISoftmax", "IllegalArgumentError", "IllegalStateError", "LLAMA_3_2_1B",
-    "LlamaConfig", "LlamaCudaError", "LlamaInference", "ModelIOError", "Session", "TINY", "default_accelerator",
-    "load_library",
+    "LlamaConfig", "LlamaCudaError", "LlamaInference", "Message", "ModelIOError", "Role", "Session",
+    "StreamDecoder", "TINY", "Tokenizer", "default_accelerator", "load_library",
 ]

@@ -66,6 +66,9 @@ class LcConfig(ctypes.Structure):
     ]
 
 
+# lc_token_callback: void (*)(int32_t token, int32_t index, void* user)
+TOKEN_CALLBACK = ctypes.CFUNCTYPE(None, c_int32, c_int32, c_void_p)
+
 # name -> (restype, argtypes).  Every symbol of include/llamacuda.h.
 SIGNATURES = {
     "lc_last_error": (c_int, [c_char_p, c_size_t]),
@@ -117,6 +120,8 @@ SIGNATURES = {
     "lc_session_destroy": (c_int, [c_void_p]),
     "lc_forward": (c_int, [c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
     "lc_generate": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int32, c_void_p, c_void_p]),
+    "lc_generate_stream": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int32, TOKEN_CALLBACK, c_void_p,
+                                   c_void_p, c_void_p]),
     "lc_decode": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     "lc_session_enable_trace": (c_int, [c_void_p, c_int32]),
     "lc_session_read_trace": (c_int, [c_void_p, c_void_p, c_int64, POINTER(c_int32), POINTER(c_int32)]),

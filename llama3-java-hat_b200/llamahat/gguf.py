@@ -6,8 +6,8 @@ The writer produces files the reference's loader accepts
 output.weight), 32-byte alignment, and -- when the vocabulary is the full
 128256 ids -- the tokenizer metadata LlamaInference's constructor reads
 (Tokenizer.java:47-95, ChatFormat.java:22-29): a gpt2 tokenizer model,
-128256 token strings with the Llama-3 special tokens at their ids, and an
-empty merges list.
+128256 token strings (byte symbols, learned merges, the Llama-3 special
+tokens at their ids) and the merge rules.
 """
 from __future__ import annotations
 
@@ -59,7 +59,11 @@ def _kv(b: bytearray, key: str, t: int, v) -> None:
 
 
 def write_gguf(path: str, cfg: LlamaConfig, weights: dict[str, np.ndarray], alignment: int = 32,
-               tokenizer: bool | None = None) -> None:
+               tokenizer=None) -> None:
+    """Writes a GGUF v3 file.  `tokenizer`: None -> the synthetic tokenizer
+    (llamahat.synth.synth_tokenizer) when the vocabulary is the full 128256
+    ids, else none; True / False force it on / off; or a (token strings,
+    merge rules) pair."""
     specs = tensor_specs(cfg)
     kv = bytearray()
     n_kv = 0
@@ -82,12 +86,16 @@ def write_gguf(path: str, cfg: LlamaConfig, weights: dict[str, np.ndarray], alig
     add("llama.attention.layer_norm_rms_epsilon", T_F32, cfg.rms_eps)
     if tokenizer is None:
         tokenizer = cfg.vocab >= 128256
+    if tokenizer is True:
+        from .synth import synth_tokenizer
+        tokenizer = synth_tokenizer(cfg.vocab)
     if tokenizer:
-        toks = [SPECIAL_TOKENS.get(i, f"<|reserved_special_token_{i}|>" if i >= 128000 else f"t{i}")
-                for i in range(cfg.vocab)]
+        toks, merges = tokenizer
+        if len(toks) != cfg.vocab:
+            raise ValueError(f"{len(toks)} token strings for a vocabulary of {cfg.vocab}")
         add("tokenizer.ggml.model", T_STRING, "gpt2")
-        add("tokenizer.ggml.tokens", T_ARRAY, (T_STRING, toks))
-        add("tokenizer.ggml.merges", T_ARRAY, (T_STRING, []))
+        add("tokenizer.ggml.tokens", T_ARRAY, (T_STRING, list(toks)))
+        add("tokenizer.ggml.merges", T_ARRAY, (T_STRING, list(merges)))
 
     info = bytearray()
     offsets = []

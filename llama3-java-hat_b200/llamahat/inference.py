@@ -43,6 +43,7 @@ class CudaModel:
             lc = cfg.to_lc()
             _lib.check(lib.lc_model_create(self.acc.handle, ctypes.byref(lc), ctypes.byref(h)))
         self.handle = h
+        self.gguf_path = gguf_path
         self._fin = weakref.finalize(self, lib.lc_model_destroy, h)
         if gguf_path is None:
             for name, a in weights.items():
@@ -81,14 +82,36 @@ class Session:
         _lib.check(lib.lc_forward(self.handle, int(token), int(pos), lp, am.ctypes.data))
         return logits, int(am[0])
 
-    def generate(self, prompt, max_new: int, stop=(EOS_TOKEN,)) -> np.ndarray:
+    def generate(self, prompt, max_new: int, stop=(EOS_TOKEN,), on_token=None) -> np.ndarray:
+        """Prefill + greedy decode in one launch.  `on_token(token, index)`,
+        when given, is called for each generated id in order while the launch
+        runs (lc_generate_stream); an exception it raises is re-raised here
+        after the launch ends."""
         lib = _lib.load()
         p = np.ascontiguousarray(np.asarray(prompt, dtype=np.int32))
         st = np.ascontiguousarray(np.asarray(sorted(stop) if stop else [], dtype=np.int32))
         out = np.zeros(max(max_new, 1), np.int32)
         n = np.zeros(1, np.int32)
-        _lib.check(lib.lc_generate(self.handle, p.ctypes.data, p.size, int(max_new),
-                                   st.ctypes.data if st.size else None, st.size, out.ctypes.data, n.ctypes.data))
+        stp = st.ctypes.data if st.size else None
+        if on_token is None:
+            _lib.check(lib.lc_generate(self.handle, p.ctypes.data, p.size, int(max_new), stp, st.size,
+                                       out.ctypes.data, n.ctypes.data))
+        else:
+            errors = []
+
+            def relay(token, index, _user):
+                if errors:
+                    return
+                try:
+                    on_token(int(token), int(index))
+                except BaseException as e:  # raised again once the C call returns
+                    errors.append(e)
+
+            cb = _lib.TOKEN_CALLBACK(relay)
+            _lib.check(lib.lc_generate_stream(self.handle, p.ctypes.data, p.size, int(max_new), stp, st.size,
+                                              cb, None, out.ctypes.data, n.ctypes.data))
+            if errors:
+                raise errors[0]
         return out[: int(n[0])].copy()
 
     def decode(self, token: int, start_pos: int, n_steps: int, out=None) -> np.ndarray:
@@ -167,12 +190,30 @@ class Batch:
 
 
 class LlamaInference:
-    """Mirror of LlamaInference (LlamaInference.java): forward / generate / argmax."""
+    """Mirror of LlamaInference (LlamaInference.java): forward / generate /
+    chat / argmax.
 
-    def __init__(self, model: CudaModel | str, acc: Accelerator | None = None, max_seq: int = 0):
+    Given a GGUF path, the constructor also builds the tokenizer and chat
+    format from the file's metadata, as the reference's does
+    (LlamaInference.java:97-99), and fails the same way when the metadata has
+    no gpt2 tokenizer.  Given a CudaModel, `tokenizer` may be passed in (or is
+    read from the model's GGUF file when it came from one); without one,
+    chat() raises IllegalStateError."""
+
+    def __init__(self, model: CudaModel | str, acc: Accelerator | None = None, max_seq: int = 0,
+                 tokenizer=None):
+        from .tokenizer import ChatFormat, Tokenizer
+        path = model if isinstance(model, str) else getattr(model, "gguf_path", None)
+        if tokenizer is None and path is not None:
+            from .gguf import read_gguf
+            meta, _ = read_gguf(path)
+            if isinstance(model, str) or meta.get("tokenizer.ggml.model") is not None:
+                tokenizer = Tokenizer.fromGGUFMetadata(meta)
         self.model = model if isinstance(model, CudaModel) else CudaModel(gguf_path=model, acc=acc, max_seq=max_seq)
         self.session = Session(self.model)
         self.cfg = self.model.cfg
+        self.tokenizer = tokenizer
+        self.chatFormat = ChatFormat(tokenizer) if tokenizer is not None else None
 
     def forward(self, token: int, pos: int) -> np.ndarray:
         """Logits [vocab] for `token` at `pos` (LlamaInference.java:117-164)."""
@@ -180,9 +221,50 @@ class LlamaInference:
         self.session.forward(token, pos, logits)
         return logits
 
-    def generate(self, promptTokens, maxNewTokens: int, stopTokens=frozenset({EOS_TOKEN})) -> np.ndarray:
-        """Greedy generation (LlamaInference.java:173-217)."""
-        return self.session.generate(promptTokens, maxNewTokens, tuple(stopTokens))
+    def generate(self, promptTokens, maxNewTokens: int, stopTokens=frozenset({EOS_TOKEN}), onToken=None) -> np.ndarray:
+        """Greedy generation (LlamaInference.java:173-217).  `onToken(token,
+        index)` streams each generated id while the launch runs."""
+        return self.session.generate(promptTokens, maxNewTokens, tuple(stopTokens), on_token=onToken)
+
+    def chat(self, systemPrompt: str | None, userPrompt: str, maxNewTokens: int, onText=None) -> str:
+        """LlamaInference.chat (LlamaInference.java:227-247): the Instruct
+        template around the prompts, greedy generation that stops at
+        <|end_of_text|> or <|eot_id|>, and the decoded text of the tokens
+        before the first stop token.  `onText(piece)` receives that text as it
+        is generated, in pieces of whole characters whose concatenation is the
+        returned string."""
+        from .tokenizer import Message, Role, StreamDecoder
+        if self.chatFormat is None:
+            raise _lib.IllegalStateError(_lib.LC_ERR_STATE, "no tokenizer: load from a GGUF file or pass tokenizer=")
+        dialog = []
+        if systemPrompt:
+            dialog.append(Message(Role.SYSTEM, systemPrompt))
+        dialog.append(Message(Role.USER, userPrompt))
+        prompt = self.chatFormat.encodeDialogPrompt(dialog)
+        stop = self.chatFormat.getStopTokens()
+        on_token = None
+        if onText is not None:
+            dec = StreamDecoder(self.tokenizer)
+            ended = [False]
+
+            def on_token(token, _index):
+                if ended[0] or token in stop:
+                    ended[0] = True
+                    return
+                piece = dec.feed(token)
+                if piece:
+                    onText(piece)
+        generated = self.session.generate(prompt, maxNewTokens, tuple(stop), on_token=on_token)
+        kept = []
+        for t in generated:
+            if int(t) in stop:
+                break
+            kept.append(int(t))
+        if onText is not None:
+            tail = dec.flush()
+            if tail:
+                onText(tail)
+        return self.tokenizer.decode(kept)
 
     @staticmethod
     def argmax(values) -> int:

@@ -21,7 +21,8 @@ headline line above):
                      shapes of the 1B model, batch 1 / 8 / 64, weight copies
                      rotated past 4x L2), RMSNorm / SwiGLU / RoPE / softmax
                      rows, GQA decode attention (batch 1 / 64, 128..8192
-                     cached positions); device time of back-to-back calls
+                     cached positions); device time of back-to-back calls;
+                     --only gemm,prefill,elementwise,attention picks sections
   --suite lmshard    (torchrun, N GPUs) lm_head rows sharded over the ranks:
                      logits slice on each GPU, then NCCL all-gather of the
                      slices or all-reduce of packed argmax keys
@@ -475,6 +476,10 @@ def run_kernels(args):
     L2 = 126 * 1024 * 1024
     peak, peak_kind = measured_peak()
     out = []
+    only = set(args.only.split(",")) if args.only else None
+
+    def want(section):
+        return only is None or section in only
 
     def emit(kind, case, us, nbytes, extra=None):
         gbs = nbytes / (us * 1e-6) / 1e9
@@ -488,7 +493,7 @@ def run_kernels(args):
     # Batched F16 products on the model's GEMV shapes (out x in).
     shapes = [(2048, 2048, "q/o"), (512, 2048, "k/v"), (8192, 2048, "gate/up"), (2048, 8192, "down"),
               (3072, 2048, "fused qkv"), (16384, 2048, "fused gate|up"), (128256, 2048, "lm_head")]
-    for rows, cols, name in shapes:
+    for rows, cols, name in (shapes if want("gemm") else []):
         wb = rows * cols * 2
         ncopy = max(1, min(256, -(-4 * L2 // wb)))
         Ws = []
@@ -528,8 +533,8 @@ def run_kernels(args):
             tpeak = float(json.load(f)["bf16_tflops"])
     except (OSError, KeyError, ValueError):
         tpeak = 1590.0
-    for rows, cols, name in [(3072, 2048, "fused qkv"), (2048, 2048, "o"), (16384, 2048, "fused gate|up"),
-                             (2048, 8192, "down")]:
+    prefill_shapes = [(3072, 2048, "fused qkv"), (2048, 2048, "o"), (16384, 2048, "fused gate|up"), (2048, 8192, "down")]
+    for rows, cols, name in (prefill_shapes if want("prefill") else []):
         M = 8192
         W = (torch.randn(rows * cols, device="cuda") * 0.02).half()
         Wt = torch.empty(rows * cols, dtype=torch.int16, device="cuda")
@@ -550,7 +555,7 @@ def run_kernels(args):
 
     # Elementwise rows (fp32 ~N(0,1)); copies rotated past 4x L2 where small.
     wn = torch.ones(2048, device="cuda")
-    for rows in (1, 64, 4096):
+    for rows in ((1, 64, 4096) if want("elementwise") else ()):
         nb = rows * 2048 * 4
         ncopy = max(1, min(64, -(-4 * L2 // nb)))
         xs = [torch.randn(rows, 2048, device="cuda") for _ in range(ncopy)]
@@ -577,7 +582,7 @@ def run_kernels(args):
 
     # GQA decode attention: 32 q heads / 8 kv heads, head_dim 64, fp32 KV,
     # one query per sequence; a call = one layer, 16 layers timed.
-    for B in (1, 64):
+    for B in ((1, 64) if want("attention") else ()):
         for L in (128, 1024, 8192):
             per_layer = B * 8 * L * 64 * 4 * 2
             ncopy = 1 if per_layer >= 4 * L2 else min(16, -(-4 * L2 // per_layer))
@@ -704,6 +709,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--suite", choices=["headline", "serving", "kernels", "lmshard"], default="headline")
+    ap.add_argument("--only", default="", help="kernels suite: comma-separated sections to run "
+                    "(gemm, prefill, elementwise, attention); default all")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

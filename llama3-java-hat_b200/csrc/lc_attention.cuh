@@ -27,7 +27,7 @@ constexpr int kAttnExactMax = 64;
 // Shared-memory floats a unit needs: q, scores, (max, sum) per head and a
 // flag word, then the cross-warp value partials of the throughput path.
 __host__ __device__ inline int attn_unit_smem_floats(int kv_mul, int tmax) {
-    return kv_mul * kAttnHeadDim + kv_mul * tmax + 2 * kv_mul + 4 + (tmax > kAttnExactMax ? 8 * kv_mul * kAttnHeadDim : 0);
+    return kv_mul * kAttnHeadDim + kv_mul * tmax + 2 * kv_mul + 4 + 8 * kv_mul * kAttnHeadDim;
 }
 
 // Partial record per (split, head): [m, l, o[64]].
@@ -148,12 +148,13 @@ __device__ __forceinline__ void attention_core_fast(const float* __restrict__ q,
 #pragma unroll
         for (int j = 0; j < 8; ++j) qr[h][j] = h < kv_mul ? qs[h * HD + 8 * sub + j] : 0.0f;
 
-    // Scores, two rounds of 32 positions in flight per warp pass.
-    for (int base = warp * 4; base < T; base += 64) {
-        float4 a[2], b[2];
-        bool ok[2];
+    // Scores, four rounds of 32 positions in flight per warp pass.
+    constexpr int R = 4;
+    for (int base = warp * 4; base < T; base += 32 * R) {
+        float4 a[R], b[R];
+        bool ok[R];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
+        for (int r = 0; r < R; ++r) {
             const int t = base + 32 * r + g;
             ok[r] = t < T;
             if (ok[r]) {
@@ -165,7 +166,7 @@ __device__ __forceinline__ void attention_core_fast(const float* __restrict__ q,
             }
         }
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
+        for (int r = 0; r < R; ++r) {
             const int t = base + 32 * r + g;
 #pragma unroll
             for (int h = 0; h < MAXH; ++h) {
@@ -212,7 +213,7 @@ __device__ __forceinline__ void attention_core_fast(const float* __restrict__ q,
     float2 acc[MAXH];
 #pragma unroll
     for (int h = 0; h < MAXH; ++h) acc[h] = make_float2(0.f, 0.f);
-#pragma unroll 4
+#pragma unroll 8
     for (int t = warp; t < T; t += 8) {
         const float2 v = __ldcg(reinterpret_cast<const float2*>(Vc + (int64_t)(t0 + t) * pos_stride) + lane);
 #pragma unroll
@@ -246,9 +247,10 @@ __device__ __forceinline__ void attention_core_fast(const float* __restrict__ q,
     }
 }
 
-// Standalone unit: attention_core (attention_core_fast<KVM> for units of
-// more than kAttnExactMax positions when KVM = kv_mul > 0), then with several
-// splits the last unit to finish (ticket on *cnt) merges the partials into out.
+// Standalone unit: attention_core (attention_core_fast<KVM>, when KVM =
+// kv_mul > 0, for units of more than kAttnExactMax positions and for every
+// unit of a sequence with several splits), then with several splits the last
+// unit to finish (ticket on *cnt) merges the partials into out.
 template <int KVM>
 __device__ __forceinline__ void attention_unit(const float* __restrict__ q, const float* __restrict__ K,
                                                const float* __restrict__ Vc, int64_t pos_stride, int t0, int t1,
@@ -257,7 +259,10 @@ __device__ __forceinline__ void attention_unit(const float* __restrict__ q, cons
                                                int tmax, float* sm) {
     constexpr int HD = kAttnHeadDim;
     const int tid = threadIdx.x;
-    if (KVM > 0 && tmax > kAttnExactMax)
+    // The exact (Java-order) path only where its result is the whole answer:
+    // one split of at most kAttnExactMax positions.  Several splits are
+    // merged anyway, so they take the throughput path.
+    if (KVM > 0 && (tmax > kAttnExactMax || nsplit > 1))
         attention_core_fast<(KVM > 0 ? KVM : 1)>(q, K, Vc, pos_stride, t0, t1, nsplit, split, out, part,
                                                  kAttnPartStride, scale, tmax, sm);
     else
@@ -273,16 +278,42 @@ __device__ __forceinline__ void attention_unit(const float* __restrict__ q, cons
         named_bar_sync(1, 256);
         if (*flag) {
             __threadfence();
+            // Loads of 8 splits at a time in flight (the merge is otherwise a
+            // chain of dependent L2 round trips); the sums still run in split
+            // order.
+            constexpr int C = 8;
             for (int hi = tid; hi < kv_mul * HD; hi += 256) {
                 const int h = hi / HD, i = hi % HD;
+                const float* p0 = part + (int64_t)h * kAttnPartStride;
+                const int64_t sstride = (int64_t)kv_mul * kAttnPartStride;
                 float M = -INFINITY;
-                for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(part + ((int64_t)s * kv_mul + h) * kAttnPartStride));
+                for (int s0 = 0; s0 < nsplit; s0 += C) {
+                    float m[C];
+#pragma unroll
+                    for (int j = 0; j < C; ++j) m[j] = s0 + j < nsplit ? __ldcg(p0 + (s0 + j) * sstride) : -INFINITY;
+#pragma unroll
+                    for (int j = 0; j < C; ++j) M = fmaxf(M, m[j]);
+                }
                 float L = 0.0f, O = 0.0f;
-                for (int s = 0; s < nsplit; ++s) {
-                    const float* pp = part + ((int64_t)s * kv_mul + h) * kAttnPartStride;
-                    const float w = exp_via_double(__fsub_rn(__ldcg(pp), M));
-                    L = fmaf(__ldcg(pp + 1), w, L);
-                    O = fmaf(__ldcg(pp + 2 + i), w, O);
+                for (int s0 = 0; s0 < nsplit; s0 += C) {
+                    float m[C], l[C], o[C];
+#pragma unroll
+                    for (int j = 0; j < C; ++j) {
+                        if (s0 + j < nsplit) {
+                            const float* pp = p0 + (s0 + j) * sstride;
+                            m[j] = __ldcg(pp);
+                            l[j] = __ldcg(pp + 1);
+                            o[j] = __ldcg(pp + 2 + i);
+                        }
+                    }
+#pragma unroll
+                    for (int j = 0; j < C; ++j) {
+                        if (s0 + j < nsplit) {
+                            const float w = exp_via_double(__fsub_rn(m[j], M));
+                            L = fmaf(l[j], w, L);
+                            O = fmaf(o[j], w, O);
+                        }
+                    }
                 }
                 out[h * HD + i] = __fdiv_rn(O, L);
             }

@@ -321,6 +321,34 @@ int lc_batch_last_ms(lc_batch* b, float* total_ms, float* decode_ms, int32_t* st
  * last lc_batch_generate. */
 int lc_batch_logits(lc_batch* b, int32_t seq, float* out);
 
+/* ------------------------------------ lm_head row shard over N GPUs ---- */
+/* The lm_head GEMV (H/LlamaInference.java:151-156) split by rows over N
+ * GPUs, one process per GPU: each rank computes its logits slice and packed
+ * argmax keys (lc_gemm_f16_tiled_argmax), then the ranks exchange only the
+ * keys; the maximum key is LlamaInference.argmax (:252-262) of the full
+ * logits.  lc_keyx does that exchange through NVLink peer memory: every
+ * rank stores its keys into every rank's mailbox and waits, bounded, for
+ * the others' flags (no library collective, no multicast).  No counterpart
+ * in the reference, which runs on one device. */
+typedef struct lc_keyx lc_keyx;
+#define LC_KEYX_HANDLE_BYTES 64
+#define LC_KEYX_MAX_WORLD 8
+
+/* Allocates this rank's mailbox for up to max_batch keys per call and
+ * writes its inter-process handle (LC_KEYX_HANDLE_BYTES bytes) to
+ * handle_out; the host gathers the handles of all ranks in rank order. */
+int lc_keyx_create(lc_context* ctx, int32_t world, int32_t rank, int32_t max_batch, lc_keyx** out,
+                   void* handle_out);
+/* Maps the other ranks' mailboxes: handles = world handles in rank order. */
+int lc_keyx_open(lc_keyx* x, const void* handles);
+/* In place: keys (device, [batch] uint64) becomes the maximum over the
+ * ranks.  Collective: every rank makes the same calls in the same order.
+ * Enqueue-only on the context's stream; a wait that gave up is reported by
+ * lc_context_synchronize (LC_ERR_TIMEOUT). */
+int lc_keyx_allreduce(lc_keyx* x, uint64_t* keys, int32_t batch);
+/* After every rank's last lc_keyx_allreduce has completed (a barrier). */
+int lc_keyx_destroy(lc_keyx* x);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1368,3 +1368,103 @@ extern "C" __attribute__((visibility("hidden"))) int lc_internal_set_error(int c
 extern "C" __attribute__((visibility("hidden"))) int lc_internal_context_device(const lc_context* c) {
     return c ? c->device : -1;
 }
+
+// ------------------------------------------------ peer key exchange ----
+
+struct lc_keyx {
+    lc_context* ctx = nullptr;
+    int world = 0, rank = 0, max_batch = 0;
+    uint8_t* mbox = nullptr;                   // this rank's mailbox (cudaMalloc)
+    void* peer[LC_KEYX_MAX_WORLD] = {};        // the other ranks' mailboxes, mapped through IPC
+    uint32_t epoch = 0;
+    bool open = false;
+};
+
+static_assert(sizeof(cudaIpcMemHandle_t) == LC_KEYX_HANDLE_BYTES, "IPC handle size");
+static_assert(LC_KEYX_MAX_WORLD == kKeyxMaxWorld, "world bound");
+
+extern "C" int lc_keyx_create(lc_context* c, int32_t world, int32_t rank, int32_t max_batch, lc_keyx** out,
+                              void* handle_out) {
+    if (!c || !out || !handle_out) return fail(LC_ERR_INVALID_ARG, "NULL argument");
+    if (world < 1 || world > LC_KEYX_MAX_WORLD || rank < 0 || rank >= world)
+        return fail(LC_ERR_INVALID_ARG, "world %d rank %d (world 1..%d)", world, rank, LC_KEYX_MAX_WORLD);
+    if (max_batch < 1 || max_batch > 4096) return fail(LC_ERR_INVALID_ARG, "max_batch %d (1..4096)", max_batch);
+    CTX_CHECK(c);
+    lc_keyx* x = new lc_keyx();
+    x->ctx = c;
+    x->world = world;
+    x->rank = rank;
+    x->max_batch = max_batch;
+    const size_t bytes = keyx_mailbox_bytes(world, max_batch);
+    cudaError_t e = cudaMalloc(&x->mbox, bytes);
+    if (e == cudaSuccess) e = cudaMemset(x->mbox, 0, bytes);
+    cudaIpcMemHandle_t h;
+    memset(&h, 0, sizeof(h));
+    if (e == cudaSuccess && world > 1) e = cudaIpcGetMemHandle(&h, x->mbox);
+    if (e != cudaSuccess) {
+        if (x->mbox) cudaFree(x->mbox);
+        delete x;
+        return cuda_fail(e, "key-exchange mailbox");
+    }
+    memcpy(handle_out, &h, sizeof(h));
+    *out = x;
+    return LC_OK;
+}
+
+extern "C" int lc_keyx_open(lc_keyx* x, const void* handles) {
+    if (!x || !handles) return fail(LC_ERR_INVALID_ARG, "NULL argument");
+    if (x->open) return fail(LC_ERR_STATE, "key exchange already open");
+    CTX_CHECK(x->ctx);
+    const uint8_t* hs = (const uint8_t*)handles;
+    for (int p = 0; p < x->world; ++p) {
+        if (p == x->rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, hs + (size_t)p * LC_KEYX_HANDLE_BYTES, sizeof(h));
+        cudaError_t e = cudaIpcOpenMemHandle(&x->peer[p], h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < p; ++q)
+                if (x->peer[q]) cudaIpcCloseMemHandle(x->peer[q]);
+            for (int q = 0; q < LC_KEYX_MAX_WORLD; ++q) x->peer[q] = nullptr;
+            return cuda_fail(e, "mapping a peer mailbox");
+        }
+    }
+    x->open = true;
+    return LC_OK;
+}
+
+extern "C" int lc_keyx_allreduce(lc_keyx* x, uint64_t* keys, int32_t batch) {
+    if (!x || !keys) return fail(LC_ERR_INVALID_ARG, "NULL argument");
+    if (!x->open) return fail(LC_ERR_STATE, "key exchange not open (lc_keyx_open)");
+    if (batch < 1 || batch > x->max_batch) return fail(LC_ERR_INVALID_ARG, "batch %d (1..%d)", batch, x->max_batch);
+    if ((uintptr_t)keys & 7) return fail(LC_ERR_INVALID_ARG, "keys must be 8-byte aligned device memory");
+    CTX_CHECK(x->ctx);
+    KeyxArgs a;
+    memset(&a, 0, sizeof(a));
+    const size_t foff = keyx_flags_offset(x->world, x->max_batch);
+    for (int p = 0; p < x->world; ++p) {
+        uint8_t* base = p == x->rank ? x->mbox : (uint8_t*)x->peer[p];
+        a.keys_mbox[p] = (uint64_t*)base;
+        a.flags_mbox[p] = (uint32_t*)(base + foff);
+    }
+    a.keys = keys;
+    a.world = x->world;
+    a.rank = x->rank;
+    a.batch = batch;
+    a.max_batch = x->max_batch;
+    a.epoch = ++x->epoch;
+    a.err = x->ctx->d_err;
+    a.timeout_ns = 2000000000ull;
+    CK(launch_keyx(a, x->ctx->stream, true), "key exchange launch");
+    return LC_OK;
+}
+
+extern "C" int lc_keyx_destroy(lc_keyx* x) {
+    if (!x) return LC_OK;
+    cudaSetDevice(x->ctx->device);
+    cudaStreamSynchronize(x->ctx->stream);
+    for (int p = 0; p < LC_KEYX_MAX_WORLD; ++p)
+        if (x->peer[p]) cudaIpcCloseMemHandle(x->peer[p]);
+    if (x->mbox) cudaFree(x->mbox);
+    delete x;
+    return LC_OK;
+}

@@ -76,6 +76,24 @@ cudaError_t launch_ex(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, 
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
 }
 
+// ---- argmax-key all-reduce over peer memory (lc_keyx.cu) ----
+constexpr int kKeyxMaxWorld = 8;
+struct KeyxArgs {
+    uint64_t* keys_mbox[kKeyxMaxWorld];   // key slots of rank p's mailbox (this rank's own included)
+    uint32_t* flags_mbox[kKeyxMaxWorld];  // flags of rank p's mailbox
+    uint64_t* keys;                       // [batch] this rank's keys in, the maximum over the ranks out
+    int world, rank, batch, max_batch;
+    uint32_t epoch;                       // call number, from 1, equal on every rank
+    int* err;
+    uint64_t timeout_ns;
+};
+// Byte offset of the flags in a mailbox ([2][world][max_batch] keys first).
+inline size_t keyx_flags_offset(int world, int max_batch) {
+    return ((size_t)2 * world * max_batch * sizeof(uint64_t) + 255) / 256 * 256;
+}
+size_t keyx_mailbox_bytes(int world, int max_batch);
+cudaError_t launch_keyx(const KeyxArgs& a, cudaStream_t st, bool pdl);
+
 // ---- fused decode step (lc_decode.cu) ----
 //
 // GEMV weights of the fused kernel live in HBM as row-group tiles: a tile is

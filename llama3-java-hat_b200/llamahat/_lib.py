@@ -126,6 +126,10 @@ SIGNATURES = {
     "lc_session_enable_trace": (c_int, [c_void_p, c_int32]),
     "lc_session_read_trace": (c_int, [c_void_p, c_void_p, c_int64, POINTER(c_int32), POINTER(c_int32)]),
     "lc_session_last_ms": (c_int, [c_void_p, POINTER(c_float)]),
+    "lc_keyx_create": (c_int, [c_void_p, c_int32, c_int32, c_int32, POINTER(c_void_p), c_void_p]),
+    "lc_keyx_open": (c_int, [c_void_p, c_void_p]),
+    "lc_keyx_allreduce": (c_int, [c_void_p, c_void_p, c_int32]),
+    "lc_keyx_destroy": (c_int, [c_void_p]),
 }
 
 _lib = None

@@ -56,3 +56,62 @@ def key_index(keys: np.ndarray) -> np.ndarray:
 def gather_logits(slices: list[np.ndarray], vocab: int) -> np.ndarray:
     """Full logits [B][vocab] from the rank-ordered slices."""
     return np.concatenate(slices, axis=1)[:, :vocab]
+
+
+KEYX_HANDLE_BYTES = 64
+
+
+class PeerKeyExchange:
+    """All-reduce (max) of packed argmax keys over NVLink peer memory
+    (lc_keyx_*): each rank stores its keys into every rank's mailbox and
+    waits, bounded, for the others' flags -- no library collective.
+
+    `gather_handles(handle: bytes) -> list[bytes]` returns every rank's
+    mailbox handle in rank order; by default torch.distributed's
+    all_gather_object on the default process group (any backend).
+    Collective: every rank constructs it, calls allreduce the same number of
+    times in the same order, and closes it after a barrier."""
+
+    def __init__(self, acc, world: int, rank: int, max_batch: int = 64, gather_handles=None):
+        import ctypes
+        from . import _lib
+        self.acc, self.world, self.rank, self.max_batch = acc, int(world), int(rank), int(max_batch)
+        lib = _lib.load()
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(KEYX_HANDLE_BYTES)
+        _lib.check(lib.lc_keyx_create(acc.handle, self.world, self.rank, self.max_batch, ctypes.byref(h), buf))
+        self.handle = h
+        try:
+            mine = bytes(buf.raw)
+            if gather_handles is None:
+                gather_handles = _torch_gather_handles
+            hs = gather_handles(mine) if self.world > 1 else [mine]
+            if len(hs) != self.world or any(len(x) != KEYX_HANDLE_BYTES for x in hs):
+                raise ValueError("gather_handles must return world handles of 64 bytes in rank order")
+            allh = ctypes.create_string_buffer(b"".join(hs), KEYX_HANDLE_BYTES * self.world)
+            _lib.check(lib.lc_keyx_open(h, allh))
+        except BaseException:
+            lib.lc_keyx_destroy(h)
+            self.handle = None
+            raise
+
+    def allreduce(self, keys, batch: int | None = None) -> None:
+        """keys: device tensor of int64 / uint64 packed keys [batch]; in
+        place, enqueued on the accelerator's stream."""
+        from . import _lib
+        n = int(batch if batch is not None else keys.numel())
+        _lib.check(_lib.load().lc_keyx_allreduce(self.handle, keys.data_ptr(), n))
+
+    def close(self) -> None:
+        from . import _lib
+        if self.handle is not None:
+            _lib.load().lc_keyx_destroy(self.handle)
+            self.handle = None
+
+
+def _torch_gather_handles(mine: bytes) -> list[bytes]:
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, mine)
+    return out
+

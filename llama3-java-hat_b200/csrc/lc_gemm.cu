@@ -274,6 +274,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         // -------------------------------------------------------- epilogue --
         griddep_wait();  // unscale and the epilogue's outputs belong to the predecessor's stream order
         const int et = threadIdx.x - kEpiT0, q4 = warp & 3, r = q4 * 32 + lane, sl = r >> 1;
+        // With one row tile a lane's row is the same in every unit: its best
+        // key over all the CTA's units goes out once, after the last unit
+        // (one global atomic per row and CTA).
+        const bool carry = p.mtiles == 1;
+        unsigned long long kcarry = 0ull;
+        bool done_all = true;
         int j = 0;
         for (int u = blockIdx.x; u < p.units; u += G, ++j) {
             // Dependents may launch once every CTA is in its last epilogue
@@ -287,8 +293,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             if (et < kGemmMaxB) bs->best[et] = 0ull;
             bool got = mbar_wait_bounded(&bs->dfull[a], (j >> 1) & 1, p.err, globaltimer_ns() + p.timeout_ns,
                                          kDevTimeoutFull);
-            if (bar_red_or(kBarEpi, 128, !got)) break;  // uniform exit
+            if (bar_red_or(kBarEpi, 128, !got)) {  // uniform exit
+                done_all = false;
+                break;
+            }
             tc_fence_after();
+            // Each row's keys come from one lead lane of the CTA (TMEM lane
+            // pair 2s, 2s + 1): its best key stays in a register.
+            unsigned long long kb = 0ull;
             for (int c0 = 0; c0 < nb; c0 += 16) {
                 uint32_t v[16];
                 tmem_ld16(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(a * kMaxN + c0), v);
@@ -301,12 +313,37 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     y[i] = (x + o) * unscale;  // even lanes: hi + lo
                 }
                 if (lead) {
-                    if (p.kspl == 1) {
+                    if (p.kspl == 1 && p.op == kGemmLogits) {
+                        // Logits of the 16 columns, then one packed key for the
+                        // chunk: its maximum (NaN never wins, padding columns
+                        // excluded) at the lowest column holding it -- the
+                        // largest of the 16 per-column keys -- except that a
+                        // NaN at global index 0 wins outright
+                        // (LlamaInference.argmax returns 0 then).
+                        const int nc = n0 + c0;
+                        if (p.logits) {
+                            float4* lo4 = reinterpret_cast<float4*>(p.logits + (size_t)s * p.ldl + nc);
+#pragma unroll
+                            for (int qd = 0; qd < 4; ++qd)
+                                lo4[qd] = make_float4(y[4 * qd], y[4 * qd + 1], y[4 * qd + 2], y[4 * qd + 3]);
+                        }
+                        float m = -INFINITY;
+#pragma unroll
+                        for (int i = 0; i < 16; ++i)
+                            if (nc + i < p.n_valid) m = fmaxf(m, y[i]);
+                        int fi = -1;
+#pragma unroll
+                        for (int i = 15; i >= 0; --i)
+                            if (nc + i < p.n_valid && y[i] == m) fi = i;
+                        unsigned long long k = fi >= 0 ? argmax_key(m, p.idx_offset + nc + fi) : 0ull;
+                        if (p.idx_offset + nc == 0 && y[0] != y[0]) k = ~0ull;
+                        kb = k > kb ? k : kb;
+                    } else if (p.kspl == 1) {
 #pragma unroll
                         for (int qd = 0; qd < 4; ++qd) {
                             float y4[4] = {y[4 * qd], y[4 * qd + 1], y[4 * qd + 2], y[4 * qd + 3]};
                             const unsigned long long k = apply4(p, s, n0 + c0 + 4 * qd, y4);
-                            if (k) atomicMax(&bs->best[sl], k);
+                            kb = k > kb ? k : kb;
                         }
                     } else {
                         float4* dst = reinterpret_cast<float4*>(p.part + ((size_t)ks * p.B + s) * p.N + n0 + c0);
@@ -316,14 +353,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     }
                 }
             }
+            if (carry) kcarry = kb > kcarry ? kb : kcarry;
+            else if (lead && kb) bs->best[sl] = kb;
             tc_fence_before();
             named_bar_sync(kBarEpi, 128);
             if (et == 0) mbar_arrive(&bs->dempty[a]);
             named_bar_sync(kBarEpi, 128);
-            if (et < kGemmMaxB && U.mt * kGemmMaxB + et < p.B && p.op == kGemmLogits && bs->best[et])
+            if (!carry && et < kGemmMaxB && U.mt * kGemmMaxB + et < p.B && p.op == kGemmLogits && bs->best[et])
                 atomicMax(p.best + U.mt * kGemmMaxB + et, bs->best[et]);
             named_bar_sync(kBarEpi, 128);
         }
+        if (carry && done_all && p.op == kGemmLogits && (r & 1) == 0 && sl < p.B && kcarry)
+            atomicMax(p.best + sl, kcarry);
     }
 
     tc_fence_before();

@@ -390,13 +390,23 @@ __global__ void __launch_bounds__(256) gemm_reduce_kernel(const __grid_constant_
         const int n = (int)(i % nq) * 4;
         const float* src = p.part + (size_t)s * p.N + n;
         const size_t stride = (size_t)p.B * p.N;
+        // Up to 8 splits' loads in flight at once (one L2 round trip instead
+        // of one per split), added in split order.
         float4 acc = __ldcg(reinterpret_cast<const float4*>(src));
-        for (int ks = 1; ks < p.kspl; ++ks) {
-            const float4 t = __ldcg(reinterpret_cast<const float4*>(src + ks * stride));
-            acc.x += t.x;
-            acc.y += t.y;
-            acc.z += t.z;
-            acc.w += t.w;
+        for (int k0 = 1; k0 < p.kspl; k0 += 8) {
+            float4 t[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (k0 + j < p.kspl) t[j] = __ldcg(reinterpret_cast<const float4*>(src + (k0 + j) * stride));
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (k0 + j < p.kspl) {
+                    acc.x += t[j].x;
+                    acc.y += t[j].y;
+                    acc.z += t[j].z;
+                    acc.w += t[j].w;
+                }
+            }
         }
         float y4[4] = {acc.x, acc.y, acc.z, acc.w};
         k = apply4(p, s, n, y4);

@@ -378,8 +378,11 @@ static int gemm_tiled(lc_context* c, const uint16_t* Wt, const float* X, float* 
     if (gemm_make_wmap(&wmap, g) != cudaSuccess || gemm_make_amap(&amap, g) != cudaSuccess)
         return fail(LC_ERR_CUDA, "tensor map encoding failed");
     cudaError_t e = dK ? cudaMemsetAsync(dK, 0, (size_t)batch * 8, c->stream) : cudaSuccess;
-    if (e == cudaSuccess) e = launch_gemm_split(dX, cols, cols, batch, As, unscale, c->stream);
-    if (e == cudaSuccess) e = launch_gemm(g, wmap, amap, c->sms, c->stream);
+    // Programmatic dependent launches: each kernel waits for its predecessor's
+    // completion before touching its data (the product streams its weights
+    // before that wait), so back-to-back calls overlap launch latency.
+    if (e == cudaSuccess) e = launch_gemm_split(dX, cols, cols, batch, As, unscale, c->stream, true);
+    if (e == cudaSuccess) e = launch_gemm(g, wmap, amap, c->sms, c->stream, true);
     return s.finish(e);
 }
 

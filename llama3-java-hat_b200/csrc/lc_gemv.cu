@@ -16,6 +16,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
                        int cols, int nseg, int* err, unsigned long long timeout_ns) {
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ int s_stop;
+    // Launched with programmatic stream serialisation: the next kernel may
+    // be scheduled now, and nothing here (weights, x, y) is touched before
+    // the predecessor has completed.
+    griddep_launch();
+    griddep_wait();
     Ring ring;
     ring.buf = smem;
     ring.full = reinterpret_cast<uint64_t*>(smem + (size_t)kStages * Geo<V>::kStageBytes);
@@ -91,9 +96,8 @@ static cudaError_t launch_v(const uint16_t* W, const float* x, float* y, int row
     const long long need = (rows + cap_rows - 1) / cap_rows;
     if (need > grid) grid = need;
     if (grid > rows) grid = rows;
-    stream_gemv_kernel<V><<<(unsigned)grid, kStreamThreads, smem, st>>>(reinterpret_cast<const __half*>(W), x, y, rows,
-                                                                      cols, nseg, err, 2000000000ull);
-    return cudaGetLastError();
+    return launch_ex(stream_gemv_kernel<V>, dim3((unsigned)grid), dim3(kStreamThreads), smem, st, true,
+                     reinterpret_cast<const __half*>(W), x, y, rows, cols, nseg, err, 2000000000ull);
 }
 
 cudaError_t launch_stream_gemv(const uint16_t* W, const float* x, float* y, int rows, int cols, int num_sms, int* err,

@@ -108,6 +108,8 @@ LC_DEV float block_sum(float v, float* red) {
 // One CTA per row: sum of squares (tree), invRms exactly as RMSNorm.java:43,
 // then x*invRms*w left to right (RMSNorm.java:48).  In place.
 __global__ void rmsnorm_rows_kernel(float* __restrict__ x, const float* __restrict__ w, int width, float eps) {
+    griddep_launch();  // programmatic dependent launch: the next kernel may be scheduled now,
+    griddep_wait();    // and nothing here is touched before the predecessor has completed
     __shared__ float red[33];
     float* row = x + (size_t)blockIdx.x * (size_t)width;
     float ss = 0.0f;
@@ -121,7 +123,7 @@ __global__ void rmsnorm_rows_kernel(float* __restrict__ x, const float* __restri
 }
 
 void launch_rmsnorm_rows(float* x, const float* w, int rows, int width, float eps, cudaStream_t st) {
-    rmsnorm_rows_kernel<<<rows, 256, 0, st>>>(x, w, width, eps);
+    launch_ex(rmsnorm_rows_kernel, dim3(rows), dim3(256), 0, st, true, x, w, width, eps);
 }
 
 // ------------------------------------------------------------------ RoPE --
@@ -135,6 +137,8 @@ void launch_rmsnorm_rows(float* x, const float* w, int rows, int width, float ep
 // the reference's uncontracted expressions, so results stay bit-identical.
 __global__ void __launch_bounds__(256) rope_rows_kernel(float* __restrict__ vec, const int32_t* __restrict__ pos,
                                                         int rows, int num_heads, int head_dim, RopeFreq fq) {
+    griddep_launch();  // programmatic dependent launch: the next kernel may be scheduled now,
+    griddep_wait();    // and nothing here is touched before the predecessor has completed
     __shared__ float2 cs[256];  // (cos, sin) per pair index; head_dim <= 512
     const int half = head_dim >> 1, width = num_heads * head_dim;
     const bool vec4 = (head_dim % 4 == 0) && ((reinterpret_cast<uintptr_t>(vec) & 15) == 0);
@@ -174,18 +178,22 @@ __global__ void __launch_bounds__(256) rope_rows_kernel(float* __restrict__ vec,
 void launch_rope_rows(float* vec, const int32_t* pos, int rows, int num_heads, int head_dim, const RopeFreq& fq,
                       cudaStream_t st) {
     const int blocks = rows < 148 * 8 ? rows : 148 * 8;
-    rope_rows_kernel<<<blocks < 1 ? 1 : blocks, 256, 0, st>>>(vec, pos, rows, num_heads, head_dim, fq);
+    launch_ex(rope_rows_kernel, dim3(blocks < 1 ? 1 : blocks), dim3(256), 0, st, true, vec, pos, rows, num_heads, head_dim, fq);
 }
 
 // ----------------------------------------------------------- SiLU/SwiGLU --
 
 __global__ void silu_kernel(float* __restrict__ x, long long n) {
+    griddep_launch();  // programmatic dependent launch: the next kernel may be scheduled now,
+    griddep_wait();    // and nothing here is touched before the predecessor has completed
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         x[i] = silu_ref(x[i]);
 }
 
 // g = silu(g) * u : SiLU.java:36-39 then TransformerBlock.elementWiseMul.
 __global__ void swiglu_kernel(float* __restrict__ g, const float* __restrict__ u, long long n) {
+    griddep_launch();  // programmatic dependent launch: the next kernel may be scheduled now,
+    griddep_wait();    // and nothing here is touched before the predecessor has completed
     const long long stride = (long long)gridDim.x * blockDim.x;
     long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const bool vec4 = ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(u)) & 15) == 0;
@@ -212,10 +220,10 @@ static int ew_blocks(long long n) {
     return b < 1 ? 1 : (int)b;
 }
 
-void launch_silu(float* x, long long n, cudaStream_t st) { silu_kernel<<<ew_blocks(n), 256, 0, st>>>(x, n); }
+void launch_silu(float* x, long long n, cudaStream_t st) { launch_ex(silu_kernel, dim3(ew_blocks(n)), dim3(256), 0, st, true, x, n); }
 
 void launch_swiglu(float* g, const float* u, long long n, cudaStream_t st) {
-    swiglu_kernel<<<ew_blocks(n), 256, 0, st>>>(g, u, n);
+    launch_ex(swiglu_kernel, dim3(ew_blocks(n)), dim3(256), 0, st, true, g, u, n);
 }
 
 // --------------------------------------------------------------- Softmax --
@@ -229,6 +237,8 @@ void launch_swiglu(float* g, const float* u, long long n, cudaStream_t st) {
 // Rows of up to 32 * EPL floats: one warp per row, EPL floats per lane.
 template <int EPL>
 __global__ void __launch_bounds__(256) softmax_rows_warp_kernel(float* __restrict__ x, int rows, int width) {
+    griddep_launch();  // programmatic dependent launch: the next kernel may be scheduled now,
+    griddep_wait();    // and nothing here is touched before the predecessor has completed
     const int lane = threadIdx.x & 31;
     const long long r = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
     if (r >= rows) return;
@@ -260,6 +270,8 @@ __global__ void __launch_bounds__(256) softmax_rows_warp_kernel(float* __restric
 // Rows of up to 256 * EPT floats: one CTA per row, EPT floats per thread.
 template <int EPT>
 __global__ void __launch_bounds__(256) softmax_rows_kernel(float* __restrict__ x, int width) {
+    griddep_launch();  // programmatic dependent launch: the next kernel may be scheduled now,
+    griddep_wait();    // and nothing here is touched before the predecessor has completed
     __shared__ float red[8];
     float* row = x + (size_t)blockIdx.x * (size_t)width;
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -300,6 +312,8 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(float* __restrict__ x
 
 // Rows wider than the register budget: max pass, exp-sum pass, write pass.
 __global__ void __launch_bounds__(256) softmax_rows_wide_kernel(float* __restrict__ x, int width) {
+    griddep_launch();  // programmatic dependent launch: the next kernel may be scheduled now,
+    griddep_wait();    // and nothing here is touched before the predecessor has completed
     __shared__ float red[8];
     float* row = x + (size_t)blockIdx.x * (size_t)width;
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -324,13 +338,13 @@ __global__ void __launch_bounds__(256) softmax_rows_wide_kernel(float* __restric
 
 void launch_softmax_rows(float* x, int rows, int width, cudaStream_t st) {
     const unsigned wgrid = (unsigned)((rows + 7) / 8);
-    if (width <= 128) softmax_rows_warp_kernel<4><<<wgrid, 256, 0, st>>>(x, rows, width);
-    else if (width <= 256) softmax_rows_warp_kernel<8><<<wgrid, 256, 0, st>>>(x, rows, width);
-    else if (width <= 512) softmax_rows_warp_kernel<16><<<wgrid, 256, 0, st>>>(x, rows, width);
-    else if (width <= 1024) softmax_rows_warp_kernel<32><<<wgrid, 256, 0, st>>>(x, rows, width);
-    else if (width <= 4096) softmax_rows_kernel<16><<<rows, 256, 0, st>>>(x, width);
-    else if (width <= 8192) softmax_rows_kernel<32><<<rows, 256, 0, st>>>(x, width);
-    else softmax_rows_wide_kernel<<<rows, 256, 0, st>>>(x, width);
+    if (width <= 128) launch_ex(softmax_rows_warp_kernel<4>, dim3(wgrid), dim3(256), 0, st, true, x, rows, width);
+    else if (width <= 256) launch_ex(softmax_rows_warp_kernel<8>, dim3(wgrid), dim3(256), 0, st, true, x, rows, width);
+    else if (width <= 512) launch_ex(softmax_rows_warp_kernel<16>, dim3(wgrid), dim3(256), 0, st, true, x, rows, width);
+    else if (width <= 1024) launch_ex(softmax_rows_warp_kernel<32>, dim3(wgrid), dim3(256), 0, st, true, x, rows, width);
+    else if (width <= 4096) launch_ex(softmax_rows_kernel<16>, dim3(rows), dim3(256), 0, st, true, x, width);
+    else if (width <= 8192) launch_ex(softmax_rows_kernel<32>, dim3(rows), dim3(256), 0, st, true, x, width);
+    else launch_ex(softmax_rows_wide_kernel, dim3(rows), dim3(256), 0, st, true, x, width);
 }
 
 // ---------------------------------------------- attention scores / values --

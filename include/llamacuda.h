@@ -170,11 +170,17 @@ int lc_attention_decode(lc_context* ctx, const float* q, const float* k, const f
  * cannot afford cudaFree's device-wide synchronisation, fixed device
  * footprint after load).  Same arguments and results as lc_attention_decode;
  * q, k, v and out must be device memory of the context's device; seq_len may
- * be host or device.  Scratch is a static 8 MiB device array per GPU (held
+ * be host memory or device memory of the context's device (another GPU's:
+ * LC_ERR_INVALID_ARG).  Scratch is a static 8 MiB device array per GPU (held
  * until exit); plans needing more, or batch > 1024, return LC_ERR_INVALID_ARG.
  * The first call on a device resolves the array's address (make it before
  * any stream capture).  All calls on a device share the array: calls that
- * overlap on the GPU race.  Enqueues on the context stream and returns. */
+ * overlap on the GPU race.  The lengths are read on the host to size the
+ * split plan: with seq_len in device memory the call first waits for the
+ * work already queued on the context stream (so lengths written there are
+ * seen), then enqueues; with seq_len in host memory it only enqueues.  In
+ * both cases it returns before the attention has run: synchronize the
+ * context before reading out. */
 int lc_attention_decode_static(lc_context* ctx, const float* q, const float* k, const float* v, float* out,
                                const int32_t* seq_len, int batch, int n_heads, int n_kv_heads, int head_dim,
                                int64_t seq_stride, int64_t head_stride, int64_t pos_stride);

@@ -66,14 +66,24 @@ void* scratch_address(int device) {
     return g_scratch_addr[device];
 }
 
-bool on_device(const void* p, int device) {
+// Where a buffer lives, as this entry point sees it.
+enum class Where { kHost, kThisDevice, kElsewhere };
+
+Where where_is(const void* p, int device) {
     cudaPointerAttributes a;
     if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
         cudaGetLastError();
-        return false;
+        return Where::kHost;  // not known to CUDA: plain host memory
     }
-    return (a.type == cudaMemoryTypeDevice && a.device == device) || a.type == cudaMemoryTypeManaged;
+    switch (a.type) {
+        case cudaMemoryTypeUnregistered:
+        case cudaMemoryTypeHost: return Where::kHost;
+        case cudaMemoryTypeManaged: return Where::kThisDevice;
+        default: return a.device == device ? Where::kThisDevice : Where::kElsewhere;
+    }
 }
+
+bool on_device(const void* p, int device) { return where_is(p, device) == Where::kThisDevice; }
 
 }  // namespace
 
@@ -108,10 +118,19 @@ extern "C" int lc_attention_decode_static(lc_context* ctx, const float* q, const
 
     // Sequence lengths: read on the host for the split plan (fixed-size stack
     // buffer, no allocation); a host array is also copied into the scratch.
+    // Lengths in device memory are read on the context stream and waited
+    // for, so values written by work queued there before this call are the
+    // ones planned with.
     int32_t hl[kStaticMaxBatch];
-    const bool lens_on_device = on_device(seq_len, device);
+    const Where lw = where_is(seq_len, device);
+    if (lw == Where::kElsewhere)
+        return lc_internal_set_error(LC_ERR_INVALID_ARG,
+                                     "seq_len is device memory of another GPU (host memory or the context's "
+                                     "device only)");
+    const bool lens_on_device = lw == Where::kThisDevice;
     if (lens_on_device) {
-        if (cudaMemcpy(hl, seq_len, (size_t)batch * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        if (cudaMemcpyAsync(hl, seq_len, (size_t)batch * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess)
             return lc_internal_set_error(LC_ERR_CUDA, "reading seq_len failed");
     } else {
         for (int b = 0; b < batch; ++b) hl[b] = seq_len[b];
@@ -140,7 +159,7 @@ extern "C" int lc_attention_decode_static(lc_context* ctx, const float* q, const
     cudaError_t e = launch_attention_decode(plan, q, k, v, out, dlens, seq_stride, head_stride, pos_stride, scratch,
                                             st);
     if (e != cudaSuccess) return lc_internal_set_error(LC_ERR_CUDA, cudaGetErrorString(e));
-    if (!lens_on_device && cudaStreamSynchronize(st) != cudaSuccess)
-        return lc_internal_set_error(LC_ERR_CUDA, "synchronize failed");
+    // The host lengths were copied out of `hl` before cudaMemcpyAsync
+    // returned (pageable source), so nothing here waits for the attention.
     return LC_OK;
 }

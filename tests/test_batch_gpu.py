@@ -166,3 +166,44 @@ def test_batch_1b_matches_oracle(acc, oracle):
     outs = Batch(model, 4).generate(prompts, 4, stop=())
     checked = sum(follow_oracle(om, p, g, 4) for p, g in zip(prompts, outs))
     assert checked >= 8
+
+
+def test_batch_1b_prefill_matches_oracle(acc, oracle):
+    """Llama-3.2-1B shapes (random weights), prompts of 129 tokens in all, so
+    they run as one prefill pass at the real dimensions: row-tiled tcgen05
+    products over all prompt rows, the causal prefill attention and K/V
+    written at (sequence, position).  The reference prefills token by token
+    (H/LlamaInference.java:186-193); every sequence must still follow the
+    oracle's greedy path and end with logits within 1e-2 of the oracle's."""
+    from llamahat import Batch, CudaModel
+    from llamahat.config import LLAMA_3_2_1B
+    from llamahat.synth import synth_weights
+    cfg = LLAMA_3_2_1B.with_(max_seq=256)
+    w = synth_weights(cfg, seed=1234)
+    model = CudaModel(cfg, w, acc=acc)
+    om = oracle.OracleModel(cfg, w)
+    rng = np.random.default_rng(4321)
+    lens = [32, 40, 7, 50]  # 129 prompt rows
+    prompts = [rng.integers(0, 128000, n).astype(np.int32) for n in lens]
+    max_new = 8
+    b = Batch(model, 4)
+    outs = b.generate(prompts, max_new, stop=())
+    checked = 0
+    for s, (p, g) in enumerate(zip(prompts, outs)):
+        assert len(g) == max_new
+        logits = None
+        for pos, t in enumerate(p):
+            logits = om.forward(int(t), pos)
+        full = True
+        for i, t in enumerate(g):
+            if top2_margin(logits) <= MARGIN:
+                full = False
+                break
+            assert int(t) == int(np.argmax(logits)), f"seq {s} token {i}: gpu {t} oracle {int(np.argmax(logits))}"
+            checked += 1
+            if i + 1 < len(g):
+                logits = om.forward(int(t), len(p) + i)
+        if full:
+            # logits that chose the last token (its forward at len(p) + max_new - 2)
+            assert np.abs(b.logits(s) - logits).max() <= LOGITS_ABS_TOL
+    assert checked >= 16

@@ -641,6 +641,7 @@ struct lc_model {
     bool has_output = false;
     bool finalized = false;
     RopeFreq rope;
+    float2* d_rope_cs = nullptr;  // [max_seq][head_dim / 2] (sin, cos) of the RoPE angles
     DecodeLaunch launch;
     int l2_prefetch_tiles = 0;    // producer L2 prefetch window (tiles)
     uint32_t* d_sched = nullptr;  // producer tile schedule (decode_build_schedule)
@@ -727,6 +728,7 @@ extern "C" int lc_model_destroy(lc_model* m) {
     if (m->d_layers) cudaFree(m->d_layers);
     if (m->d_sched) cudaFree(m->d_sched);
     if (m->d_sched_n) cudaFree(m->d_sched_n);
+    if (m->d_rope_cs) cudaFree(m->d_rope_cs);
     delete m;
     return LC_OK;
 }
@@ -891,7 +893,12 @@ static void fill_model_params(const lc_model* m, DecodeParams* p) {
     p->lm_head = m->lm_tiled;  // output.weight, or the tied embedding (LlamaInference.java:69-72)
     p->out_norm = m->out_norm;
     p->layers = m->d_layers;
+    for (int l = 0; l < c.n_layers && l < kMaxDecodeLayers; ++l) {
+        p->norm_w[2 * l] = m->layers[l].attn_norm;
+        p->norm_w[2 * l + 1] = m->layers[l].ffn_norm;
+    }
     p->rope = m->rope;
+    p->rope_cs = m->d_rope_cs;
     p->timeout_ns = 2000000000ull;
     p->sched = m->d_sched;
     p->sched_n = m->d_sched_n;
@@ -922,6 +929,19 @@ extern "C" int lc_model_finalize(lc_model* m) {
     m->staging = nullptr;
     m->staging_bytes = 0;
     make_rope_freq(&m->rope, m->cfg.rope_theta, m->cfg.head_dim);
+    {
+        // The rotation of pair i at position pos (RoPE.java:42-46): the float
+        // angle pos * freq, its sine and cosine in double, rounded to float.
+        const int half = m->cfg.head_dim / 2;
+        std::vector<float2> cs((size_t)m->cfg.max_seq * half);
+        for (int pos = 0; pos < m->cfg.max_seq; ++pos)
+            for (int i = 0; i < half; ++i) {
+                const float val = (float)pos * m->rope.f[i];
+                cs[(size_t)pos * half + i] = make_float2((float)sin((double)val), (float)cos((double)val));
+            }
+        CK(cudaMalloc(&m->d_rope_cs, cs.size() * sizeof(float2)), "rope table");
+        CK(cudaMemcpy(m->d_rope_cs, cs.data(), cs.size() * sizeof(float2), cudaMemcpyHostToDevice), "rope table");
+    }
     if (const char* e = getenv("LLAMACUDA_L2_PREFETCH_TILES")) m->l2_prefetch_tiles = atoi(e);
     std::vector<LayerW> lw(m->cfg.n_layers);
     for (int l = 0; l < m->cfg.n_layers; ++l) {

@@ -56,6 +56,7 @@ void decode_build_schedule(const DecodeParams& p, const LayerW* layers, int G, s
 bool decode_plan(const DecodeParams& p, int num_sms, DecodeLaunch* out, const char** why) {
     const int qdim = p.n_heads * p.head_dim, kv_mul = p.n_heads / p.n_kv;
     if (p.head_dim != kAttnHeadDim) return *why = "fused decode implements head_dim 64", false;
+    if (p.n_layers > kMaxDecodeLayers) return *why = "fused decode implements at most 64 layers", false;
     if (p.dim != 256 && p.dim != 512 && p.dim != 1024 && p.dim != 2048)
         return *why = "fused decode implements dim 256, 512, 1024 or 2048", false;
     if (qdim != p.dim) return *why = "fused decode needs n_heads * head_dim == dim", false;
@@ -66,6 +67,7 @@ bool decode_plan(const DecodeParams& p, int num_sms, DecodeLaunch* out, const ch
     if (p.hidden / p.dim > kBatchTiles) return *why = "fused decode needs hidden <= 8 * dim", false;
     if (p.hidden > 8 * 4 * kCT) return *why = "fused decode implements hidden <= 8192", false;
     if (attn_scratch_floats(kv_mul) > kActFloats) return *why = "fused decode attention scratch exceeds its region", false;
+    if (kv_mul * kAttnHeadDim > kBatchTiles * 8 * kCW) return *why = "fused decode q staging exceeds its region", false;
     const Layout L = finish_layout(make_layout(p.dim));
     if (L.total > 227 * 1024) return *why = "fused decode shared-memory plan exceeds 227 KB", false;
     out->grid = num_sms;

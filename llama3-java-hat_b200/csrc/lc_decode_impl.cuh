@@ -91,10 +91,9 @@ __host__ __device__ inline int attn_split_len(int seq, int G, int n_kv) {
     return T;
 }
 
-// q, this position's k and v, K/V chunk, scores, per-head (max, sum).
-__host__ __device__ inline int attn_scratch_floats(int kv_mul) {
-    return kv_mul * (kAttnHeadDim + kAttnTmax) + 2 * kAttnHeadDim + kVChunk * kAttnHeadDim + 16;
-}
+// Attention scratch in the act region: a K chunk and a V chunk (q and the
+// probabilities sit in the ys region, see attn_unit).
+__host__ __device__ inline int attn_scratch_floats(int /*kv_mul*/) { return 2 * kVChunk * kAttnHeadDim; }
 
 struct Shared {
     int stop;       // consumers -> producer: leave
@@ -315,20 +314,12 @@ __device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uin
 // 2^-22 relative (the subtraction is exact: hi is x rounded to 11 bits).
 // One scale per vector (max |x| * 2^e in [2^14, 2^15)) keeps both parts in
 // range; 2^-e goes to sh->unscale.  The thread's values v[k] are the float4
-// at index idx[k] of the vector (idx < 0: none).  Ends with a barrier.
-// `ok` is the thread's status so far; returns the CTA-uniform AND of it.
+// at index idx[k] of the vector (idx < 0: none).  split_store takes the
+// vector's maximum |x| m (to within an ulp or two; the same in every thread)
+// and ends with a barrier.
 template <int NV>
-__device__ __forceinline__ bool stage_split(const Smem& sm, const float4 (&v)[NV], const int (&idx)[NV], bool ok) {
-    const int tid = threadIdx.x, warp = tid >> 5;
-    float m = 0.0f;
-#pragma unroll
-    for (int k = 0; k < NV; ++k)
-        if (idx[k] >= 0) m = fmaxf(m, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
-    m = warp_max(m);
-    if ((tid & 31) == 0) sm.sh->rmax[warp] = m;
-    ok = !bar_red_or(kBarC, kCT, !ok);
-#pragma unroll
-    for (int k = 0; k < kCW; ++k) m = fmaxf(m, sm.sh->rmax[k]);
+__device__ __forceinline__ void split_store(const Smem& sm, const float4 (&v)[NV], const int (&idx)[NV], float m) {
+    const int tid = threadIdx.x;
     int e = 0;
     if (m > 0.0f) {
         e = 14 - (((__float_as_int(m) >> 23) & 0xff) - 127);
@@ -346,6 +337,23 @@ __device__ __forceinline__ bool stage_split(const Smem& sm, const float4 (&v)[NV
         }
     }
     named_bar_sync(kBarC, kCT);
+}
+
+// The maximum of the vector first (one reduction round), then split_store.
+// `ok` is the thread's status so far; returns the CTA-uniform AND of it.
+template <int NV>
+__device__ __forceinline__ bool stage_split(const Smem& sm, const float4 (&v)[NV], const int (&idx)[NV], bool ok) {
+    const int tid = threadIdx.x, warp = tid >> 5;
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+        if (idx[k] >= 0) m = fmaxf(m, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
+    m = warp_max(m);
+    if ((tid & 31) == 0) sm.sh->rmax[warp] = m;
+    ok = !bar_red_or(kBarC, kCT, !ok);
+#pragma unroll
+    for (int k = 0; k < kCW; ++k) m = fmaxf(m, sm.sh->rmax[k]);
+    split_store<NV>(sm, v, idx, m);
     return ok;
 }
 
@@ -719,11 +727,13 @@ __device__ __forceinline__ float row_sum(const float* ys, int ng, int ncb, int g
     return y;
 }
 
-// RoPE of one interleaved pair (RoPE.java:42-49) at position pos.
-__device__ __forceinline__ void rope_pair(float& v0, float& v1, int pos, float freq) {
-    double sd, cd;
-    sincos((double)__fmul_rn((float)pos, freq), &sd, &cd);
-    const float2 sc = make_float2((float)sd, (float)cd);
+// x / (1 + exp(-x)) (SiLU.java:36-39) with the single-precision exponential:
+// within two ulp of the reference's double-precision one.
+__device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+
+// RoPE of one interleaved pair (RoPE.java:42-49); sc = (sin, cos) of the
+// pair's angle at this position, from the model's table.
+__device__ __forceinline__ void rope_pair(float& v0, float& v1, float2 sc) {
     const float a = v0, b = v1;
     v0 = __fsub_rn(__fmul_rn(a, sc.y), __fmul_rn(b, sc.x));
     v1 = __fadd_rn(__fmul_rn(a, sc.x), __fmul_rn(b, sc.y));
@@ -750,7 +760,7 @@ __device__ __forceinline__ void epilogue(const DecodeParams& p, const Smem& sm, 
             // q rows, then k rows, then v rows; k and q are rotated.
             const int kv = R < qdim ? -1 : (R < qdim + kvd ? 0 : 1);
             const int rr = R - (kv < 0 ? 0 : qdim + kv * kvd), i = rr & (HD - 1);
-            if (kv <= 0) rope_pair(y0, y1, pos, p.rope.f[i >> 1]);
+            if (kv <= 0) rope_pair(y0, y1, __ldg(p.rope_cs + (size_t)pos * (HD / 2) + (i >> 1)));
             if (kv < 0) {
                 st_tag2(p.q + R, y0, y1, tg);
             } else {
@@ -765,8 +775,8 @@ __device__ __forceinline__ void epilogue(const DecodeParams& p, const Smem& sm, 
         // rows 4m..4m+3 = (gate, up) of h[2m], h[2m+1] (TransformerBlock.java:205-209)
         for (int pi = tid; pi < nrows / 4; pi += kCT) {
             const int gg = pi >> 1, r = (pi & 1) * 4, R = (b0 + gg) * 8 + r;
-            const float h0 = __fmul_rn(silu_ref(row_sum(sm.ys, ng, 1, gg, r)), row_sum(sm.ys, ng, 1, gg, r + 1));
-            const float h1 = __fmul_rn(silu_ref(row_sum(sm.ys, ng, 1, gg, r + 2)), row_sum(sm.ys, ng, 1, gg, r + 3));
+            const float h0 = __fmul_rn(silu_f(row_sum(sm.ys, ng, 1, gg, r)), row_sum(sm.ys, ng, 1, gg, r + 1));
+            const float h1 = __fmul_rn(silu_f(row_sum(sm.ys, ng, 1, gg, r + 2)), row_sum(sm.ys, ng, 1, gg, r + 3));
             *reinterpret_cast<float2*>(p.h + (R >> 1)) = make_float2(h0, h1);
         }
     } else if (kind == kLM) {
@@ -925,180 +935,198 @@ __device__ __forceinline__ bool consume_job(const DecodeParams& p, const Smem& s
 // ------------------------------------------------------------- consumer --
 
 // One attention unit: positions [t0, t1) of kv head kvh for its kv_mul query
-// heads at position pos.  Same arithmetic as attention_core
-// (lc_attention.cuh), so a single split is bit-identical to the Java kernels:
-// sequential score dot products (Attention.java:36-40), max, exp in double,
-// sequential sum, p = e * (1/sum) (Softmax.java:30-50), sequential weighted
-// values (Attention.java:54-60).  K rows of earlier positions (plain fp32
-// cache, written at earlier positions) are requested before the wait for
-// this position's q, k and v (tagged words), which waits only for the CTAs
-// that own those rows of the QKV job (rotation `qkv_shift`).  K, then V,
-// pass through shared memory kVChunk positions at a time.
+// heads at position pos (TransformerBlock.java:153-192 with
+// Attention.java:32-61 and Softmax.java:28-51), written for latency.  The
+// positions go through an online softmax in chunks of kVChunk.  With
+// kv_mul <= 4 two warps serve each query head: warp (h, dp) scores positions
+// [32 dp, 32 dp + 32) of the chunk, one per lane, the pair exchanges its
+// chunk maximum and sum through a 64-thread named barrier, and each warp
+// then produces dims [32 dp, 32 dp + 32) from the chunk's probabilities in
+// shared memory.  With kv_mul > 4 one warp serves a head (two positions and
+// two dims per lane, probabilities by shuffle).  Scores use four independent
+// FMA chains over a K chunk held swizzled in shared memory (conflict-free
+// row reads); values use eight.  K and V rows of earlier positions (plain
+// fp32 cache, written at earlier positions) are requested into registers
+// before the wait for this position's q, k and v (tagged words), and the
+// next chunk's rows while the current one is computed.  One split writes the
+// normalised output; several write (max, sum, unnormalised output) partials
+// for the merge in stage_att.
 __device__ __forceinline__ bool attn_unit(const DecodeParams& p, int s, int l, int pos, int kvh, int t0, int t1,
-                                          int nsplit, int sp, int qkv_shift, float* sm, Tracer& tr) {
-    constexpr int HD = kAttnHeadDim, VPT = kVChunk * HD / 4 / kCT;  // float4 of a chunk per thread
+                                          int nsplit, int sp, const Smem& smv, Tracer& tr) {
+    constexpr int HD = kAttnHeadDim, C = kVChunk;
+    constexpr int NF4 = C * (HD / 4) / kCT;  // float4 of a K (and of a V) chunk per thread
+    static_assert(NF4 * kCT == C * (HD / 4), "chunk must divide over the consumer threads");
+    static_assert(C == 64 && HD == 64, "two lanes' worth of positions and dims per warp");
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kv_mul = p.n_heads / p.n_kv, T = t1 - t0, pr = pos - t0;  // pr: row of pos in the unit
     const int kvd = p.n_kv * HD;
+    const bool pair = kv_mul <= kCW / 2;  // two warps per query head
+    const int h = pair ? warp >> 1 : warp, dp = pair ? warp & 1 : 0;
+    const bool active = h < kv_mul;
     const uint32_t in_tag = xtag(p, s, 5 * l + 0), out_tag = xtag(p, s, 5 * l + 1);
-    float* qs = sm;
-    float* cur = qs + kv_mul * HD;  // this position's k, v
-    float* kvs = cur + 2 * HD;
-    float* sc = kvs + kVChunk * HD;
-    float* st = sc + kv_mul * kAttnTmax;
     const size_t kvbase = (((size_t)l * p.n_kv + kvh) * p.max_seq + t0) * HD;
     const float4* K4 = reinterpret_cast<const float4*>(p.kcache + kvbase);
     const float4* V4 = reinterpret_cast<const float4*>(p.vcache + kvbase);
-    // Rows [c0, c0 + n) of K or V (cache, without row pos) -> kvs, by threads
-    // t0th.. of the CTA: all loads in flight, then the stores.
-    auto load_rows = [&](const float4* src, int c0, int t0th) {
-        constexpr int R = (kVChunk * HD / 4 + kCT - 32 - 1) / (kCT - 32);  // float4 per thread, at most
-        const int n4 = min(kVChunk, T - c0) * (HD / 4), step = kCT - t0th, i0 = tid - t0th;
-        float4 r[R];
+    float4* Ks4 = reinterpret_cast<float4*>(smv.act);  // [C][16] float4, slot j ^ (row & 15)
+    float4* Vs4 = Ks4 + C * (HD / 4);                   // [C][16] float4
+    const float* Vs = reinterpret_cast<const float*>(Vs4);
+    float* qs = smv.ys;                                 // [kv_mul][HD]
+    float* ps = smv.ys + (kCW / 2) * HD;                // [kv_mul][C] probabilities (pair mode)
+    float4 kr[NF4], vr[NF4];
+    // Cache rows [c0, c0 + C) of the unit into registers (row pos excluded).
+    auto fetch = [&](int c0) {
+        const int n4 = min(C, T - c0) * (HD / 4);
 #pragma unroll
-        for (int k = 0; k < R; ++k) {
-            const int i = i0 + k * step;
-            if (i0 >= 0 && i < n4 && c0 + i / (HD / 4) != pr) r[k] = __ldcg(src + (size_t)c0 * (HD / 4) + i);
-        }
-#pragma unroll
-        for (int k = 0; k < R; ++k) {
-            const int i = i0 + k * step;
-            if (i0 >= 0 && i < n4 && c0 + i / (HD / 4) != pr) reinterpret_cast<float4*>(kvs)[i] = r[k];
+        for (int k = 0; k < NF4; ++k) {
+            const int f = tid + k * kCT;
+            if (f < n4 && c0 + (f >> 4) != pr) {
+                kr[k] = __ldcg(K4 + (size_t)c0 * (HD / 4) + f);
+                vr[k] = __ldcg(V4 + (size_t)c0 * (HD / 4) + f);
+            }
         }
     };
-    // Row pos of the chunk at c0 from cur (k: which = 0, v: 1).
-    auto put_cur = [&](int c0, int which) {
-        if (pr >= c0 && pr < c0 + kVChunk && tid < HD / 4)
-            reinterpret_cast<float4*>(kvs)[(pr - c0) * (HD / 4) + tid] =
-                reinterpret_cast<const float4*>(cur + which * HD)[tid];
-    };
-    load_rows(K4, 0, 32);  // warp 0 starts on q / k / v at once
+    fetch(0);
     bool ok = true;
     tr.mark();
-    // q and this position's k, v (tagged), one float4 per thread; the first
-    // V chunk (cache rows) in registers meanwhile.
+    // q of the kv head's query heads and this position's k, v: one float4
+    // of tagged words per thread; q goes to shared memory, k and v stay in
+    // the gathering threads' registers until their chunk is staged.
+    const int nq = kv_mul * (HD / 4), cj = tid - nq;  // cj in [0, 32): k (< 16) or v chunk j of row pos
+    float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
     {
-        const int nq = kv_mul * HD / 4;
         const uint64_t* src = nullptr;
-        float* dst = nullptr;
-        if (tid < nq) {
-            src = p.q + ((size_t)kvh * kv_mul * HD + 4 * tid);
-            dst = qs + 4 * tid;
-        } else if (tid < nq + HD / 2) {
-            const int j = tid - nq, which = j / (HD / 4), e = (j % (HD / 4)) * 4;
-            src = p.kv + (size_t)which * kvd + kvh * HD + e;
-            dst = cur + which * HD + e;
-        }
+        if (tid < nq) src = p.q + ((size_t)kvh * kv_mul * HD + 4 * tid);
+        else if (cj < HD / 2) src = p.kv + (size_t)(cj >> 4) * kvd + kvh * HD + (cj & 15) * 4;
         if (src) {
             const int one[1] = {0};
             float4 v[1];
             ok = gather_tagged<1>(p, src, one, in_tag, v) && ok;
-            *reinterpret_cast<float4*>(dst) = v[0];
+            g = v[0];
         }
+        if (tid < nq) reinterpret_cast<float4*>(qs)[tid] = g;
     }
-    float4 vr[VPT];
-    {
-        const int n4 = min(kVChunk, T) * (HD / 4);
+    float m = -INFINITY, lsum = 0.0f;
+    float acc[2][8];  // [dim of the lane][chain]
 #pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-            const int i = tid + k * kCT;
-            if (i < n4 && i / (HD / 4) != pr) vr[k] = __ldcg(V4 + i);
-        }
-    }
-    ok = !bar_red_or(kBarC, kCT, !ok);
-    // Scores, chunk by chunk: consecutive threads take the kv_mul heads of one position.
-    for (int c0 = 0; c0 < T; c0 += kVChunk) {
-        if (c0 > 0) {
-            named_bar_sync(kBarC, kCT);  // previous chunk's scores done
-            load_rows(K4, c0, 0);
-        }
-        put_cur(c0, 0);
-        named_bar_sync(kBarC, kCT);
-        const int n = min(kVChunk, T - c0);
-        for (int idx = tid; idx < n * kv_mul; idx += kCT) {
-            const int h = idx % kv_mul, tt = idx / kv_mul;
-            const float* kr = kvs + tt * HD;
-            const float* qh = qs + h * HD;
-            float sum = 0.0f;
-#pragma unroll 16
-            for (int i = 0; i < HD; ++i) sum = __fadd_rn(sum, __fmul_rn(qh[i], kr[i]));
-            sc[h * kAttnTmax + c0 + tt] = __fmul_rn(sum, p.attn_scale);
-        }
-    }
-    tr.mark();
-    named_bar_sync(kBarC, kCT);
-    // Per head: max, e = exp(s - max), sum.  The first V chunk replaces K.
-    {
-        const int n4 = min(kVChunk, T) * (HD / 4);
+    for (int d = 0; d < 2; ++d)
 #pragma unroll
-        for (int k = 0; k < VPT; ++k) {
-            const int i = tid + k * kCT;
-            if (i < n4 && i / (HD / 4) != pr) reinterpret_cast<float4*>(kvs)[i] = vr[k];
+        for (int c = 0; c < 8; ++c) acc[d][c] = 0.0f;
+    const float4* q4 = reinterpret_cast<const float4*>(qs + h * HD);
+    const int i0 = pair ? dp * 32 + lane : lane;  // the lane's dim (one warp per head: also i0 + 32)
+    const uint32_t pbar = 2u + (uint32_t)h;       // named barrier of the head's warp pair
+    for (int c0 = 0; c0 < T; c0 += C) {
+        const int n = min(C, T - c0);
+        if (c0 > 0) named_bar_sync(kBarC, kCT);  // the previous chunk's reads are done
+#pragma unroll
+        for (int k = 0; k < NF4; ++k) {
+            const int f = tid + k * kCT, row = f >> 4, j = f & 15;
+            if (row < n && c0 + row != pr) {
+                Ks4[row * 16 + (j ^ (row & 15))] = kr[k];
+                Vs4[f] = vr[k];
+            }
         }
-        put_cur(0, 1);
-    }
-    for (int h = warp; h < kv_mul; h += kCW) {
-        float* e = sc + h * kAttnTmax;
-        float m = -INFINITY;
-        for (int t = lane; t < T; t += 32) m = fmaxf(m, e[t]);
-        m = warp_max(m);
-        for (int t = lane; t < T; t += 32) e[t] = exp_via_double(__fsub_rn(e[t], m));
-        __syncwarp();
-        float lsum = 0.0f;
-        if (nsplit == 1) {
-            if (lane == 0)
-                for (int t = 0; t < T; ++t) lsum = __fadd_rn(lsum, e[t]);
-            lsum = __shfl_sync(0xffffffffu, lsum, 0);
+        if (cj >= 0 && cj < HD / 2 && pr >= c0 && pr < c0 + C) {
+            const int row = pr - c0, j = cj & 15;
+            if (cj < 16) Ks4[row * 16 + (j ^ (row & 15))] = g;
+            else Vs4[row * 16 + j] = g;
+        }
+        if (c0 == 0) {
+            ok = !bar_red_or(kBarC, kCT, !ok);
+            tr.mark();
         } else {
-            for (int t = lane; t < T; t += 32) lsum += e[t];
-            lsum = warp_sum(lsum);
-        }
-        if (lane == 0) {
-            st[2 * h] = m;
-            st[2 * h + 1] = lsum;
-        }
-    }
-    named_bar_sync(kBarC, kCT);
-    tr.mark();
-    // Weighted values: thread per (head, dim), sequential over positions.
-    float acc[2] = {0.0f, 0.0f};  // kv_mul * HD <= 2 * kCT
-    for (int c0 = 0; c0 < T; c0 += kVChunk) {
-        if (c0 > 0) {
-            named_bar_sync(kBarC, kCT);  // previous chunk fully read
-            load_rows(V4, c0, 0);
-            put_cur(c0, 1);
             named_bar_sync(kBarC, kCT);
         }
-        const int n = min(kVChunk, T - c0);
+        if (c0 + C < T) fetch(c0 + C);
+        if (active && ok) {
+            // Scores of the lane's positions.
+            float sc[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int hi = tid + k * kCT;
-            if (hi < kv_mul * HD) {
-                const int h = hi / HD, i = hi % HD;
-                const float* e = sc + h * kAttnTmax + c0;
-                float a = acc[k];
-                if (nsplit == 1) {
-                    const float inv = __fdiv_rn(1.0f, st[2 * h + 1]);
-                    for (int t = 0; t < n; ++t) a = __fadd_rn(a, __fmul_rn(__fmul_rn(e[t], inv), kvs[t * HD + i]));
-                } else {
-                    for (int t = 0; t < n; ++t) a = fmaf(e[t], kvs[t * HD + i], a);
+            for (int k = 0; k < 2; ++k) {
+                if (pair && k == 1) break;
+                const int t = pair ? dp * 32 + lane : lane + 32 * k;
+                if (t < n) {
+                    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+                    for (int j = 0; j < HD / 4; ++j) {
+                        const float4 kk = Ks4[t * 16 + (j ^ (t & 15))], qq = q4[j];
+                        a0 = fmaf(qq.x, kk.x, a0);
+                        a1 = fmaf(qq.y, kk.y, a1);
+                        a2 = fmaf(qq.z, kk.z, a2);
+                        a3 = fmaf(qq.w, kk.w, a3);
+                    }
+                    sc[k] = ((a0 + a1) + (a2 + a3)) * p.attn_scale;
                 }
-                acc[k] = a;
+            }
+            float mc = warp_max(fmaxf(sc[0], sc[1]));
+            if (pair) {
+                if (lane == 0) smv.sh->rmax[warp] = mc;
+                named_bar_sync(pbar, 64);
+                mc = fmaxf(smv.sh->rmax[warp & ~1], smv.sh->rmax[warp | 1]);
+            }
+            const float mn = fmaxf(m, mc);
+            const float rs = (m == -INFINITY) ? 0.0f : expf(m - mn);
+            const float e0 = sc[0] == -INFINITY ? 0.0f : expf(sc[0] - mn);
+            const float e1 = sc[1] == -INFINITY ? 0.0f : expf(sc[1] - mn);
+            float es = warp_sum(e0 + e1);
+            if (pair) {
+                ps[h * C + dp * 32 + lane] = e0;
+                if (lane == 0) smv.sh->red[warp] = es;
+                named_bar_sync(pbar, 64);
+                es = smv.sh->red[warp & ~1] + smv.sh->red[warp | 1];
+            }
+            lsum = fmaf(lsum, rs, es);
+            m = mn;
+#pragma unroll
+            for (int d = 0; d < 2; ++d)
+#pragma unroll
+                for (int c = 0; c < 8; ++c) acc[d][c] *= rs;
+            // Weighted values.
+            if (pair) {
+                const float* prow = ps + h * C;
+                const float* vcol = Vs + i0;
+                for (int t8 = 0; t8 < n; t8 += 8) {
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const int t = t8 + c;
+                        const float vv = t < n ? vcol[t * HD] : 0.0f;
+                        acc[0][c] = fmaf(prow[t], vv, acc[0][c]);  // prow[t] is 0 past n
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    const float ek = k == 0 ? e0 : e1;
+                    for (int t8 = 32 * k; t8 < min(n, 32 * k + 32); t8 += 8) {
+#pragma unroll
+                        for (int c = 0; c < 8; ++c) {
+                            const int t = t8 + c;
+                            const float pt = __shfl_sync(0xffffffffu, ek, t & 31);
+                            const float v0 = t < n ? Vs[t * HD + i0] : 0.0f;
+                            const float v1 = t < n ? Vs[t * HD + i0 + 32] : 0.0f;
+                            acc[0][c] = fmaf(pt, v0, acc[0][c]);
+                            acc[1][c] = fmaf(pt, v1, acc[1][c]);
+                        }
+                    }
+                }
             }
         }
     }
+    tr.mark();
+    if (active && ok) {
+        const float inv = __fdiv_rn(1.0f, lsum);
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-        const int hi = tid + k * kCT;
-        if (hi < kv_mul * HD) {
-            const int h = hi / HD, i = hi % HD;
+        for (int d = 0; d < 2; ++d) {
+            if (d == 1 && pair) break;
+            const int i = i0 + 32 * d;
+            const float o = ((acc[d][0] + acc[d][1]) + (acc[d][2] + acc[d][3])) +
+                            ((acc[d][4] + acc[d][5]) + (acc[d][6] + acc[d][7]));
             if (nsplit == 1) {
-                st_tag1(p.att + ((size_t)kvh * kv_mul + h) * HD + i, acc[k], out_tag);
+                st_tag1(p.att + ((size_t)kvh * kv_mul + h) * HD + i, __fmul_rn(o, inv), out_tag);
             } else {
                 uint64_t* pp = p.part + (((size_t)kvh * p.attn_max_splits + sp) * kv_mul + h) * kDecodePartStride;
-                st_tag1(pp + 4 + i, acc[k], out_tag);
+                st_tag1(pp + 4 + i, o, out_tag);
                 if (i == 0) {
-                    st_tag2(pp, st[2 * h], st[2 * h + 1], out_tag);
+                    st_tag2(pp, m, lsum, out_tag);
                     st_tag2(pp + 2, 0.0f, 0.0f, out_tag);
                 }
             }
@@ -1110,7 +1138,7 @@ __device__ __forceinline__ bool attn_unit(const DecodeParams& p, int s, int l, i
 // Attention units of layer l at position pos: unit u = (kv head, split) runs
 // on CTA u * G / units.
 __device__ __forceinline__ bool run_attention(const DecodeParams& p, const Smem& sm, int s, int l, int pos,
-                                              int qkv_shift, Tracer& tr) {
+                                              Tracer& tr) {
     const int G = gridDim.x, cta = blockIdx.x, seq = pos + 1;
     const int T = attn_split_len(seq, G, p.n_kv), nsplit = (seq + T - 1) / T, units = p.n_kv * nsplit;
     bool ok = true;
@@ -1119,7 +1147,7 @@ __device__ __forceinline__ bool run_attention(const DecodeParams& p, const Smem&
     for (int u = (cta * units + G - 1) / G; u < units && (u * G) / units == cta; ++u) {
         const int kvh = u / nsplit, sp = u % nsplit;
         const int t0 = sp * T, t1 = min(seq, t0 + T);
-        ok &= attn_unit(p, s, l, pos, kvh, t0, t1, nsplit, sp, qkv_shift, sm.act, tr);
+        ok &= attn_unit(p, s, l, pos, kvh, t0, t1, nsplit, sp, sm, tr);
         named_bar_sync(kBarC, kCT);
         tr.mark();
     }
@@ -1227,7 +1255,6 @@ __device__ __forceinline__ void run_consumer(const DecodeParams& p, const Smem& 
     }
 #endif
     Rotation rot;
-    int qkv_shift = 0;  // rotation of the current layer's QKV job
     RingPos ring;
     ring.slot = 0;
     ring.par = 0;
@@ -1258,13 +1285,11 @@ __device__ __forceinline__ void run_consumer(const DecodeParams& p, const Smem& 
 #pragma unroll 1
         for (int j = 0; j < njobs; ++j) {
             const int kind = (j == 4 * NL) ? (int)kLM : (j & 3), l = (j == 4 * NL) ? NL - 1 : (j >> 2);
-            const LayerW* LW = p.layers + l;
             // Exchange this job waits for: the previous job's output.
             const uint32_t want = xtag(p, s, 5 * l + (kind == kQKV ? -1 : kind == kO ? 1 : kind == kGU ? 2 : kind == kDN ? 3 : 4));
             tr.mark();
             const JobGeo jg = job_geo(p, p.layers, kind, l);
             int g0, g1;
-            if (kind == kQKV) qkv_shift = rot.shift;
             job_range(jg.groups, 1, G, rot.rank(cta, G), &g0, &g1);
             rot.advance(jg.groups, 1, G);
             if (kind == kO) {
@@ -1273,7 +1298,7 @@ __device__ __forceinline__ void run_consumer(const DecodeParams& p, const Smem& 
                 ok &= stage_h(p, sm, want, tr);
             } else {
                 const bool first = (kind == kQKV && l == 0);
-                const float* w = (kind == kQKV) ? LW->attn_norm : (kind == kGU) ? LW->ffn_norm : p.out_norm;
+                const float* w = (kind == kQKV) ? p.norm_w[2 * l] : (kind == kGU) ? p.norm_w[2 * l + 1] : p.out_norm;
                 // x after O for GU, after DN (previous layer) for QKV and LM
                 ok &= stage_norm(p, sm, first ? nullptr : (kind == kGU ? p.xa : p.xb), emb, w, want, tr);
             }
@@ -1295,7 +1320,7 @@ __device__ __forceinline__ void run_consumer(const DecodeParams& p, const Smem& 
                 publish(p, out_tag, kind == kGU);  // h is plain fp32: fenced
                 if (kind == kQKV) {
                     tr.mark();
-                    ok &= run_attention(p, sm, s, l, pos, qkv_shift, tr);
+                    ok &= run_attention(p, sm, s, l, pos, tr);
                     publish(p, xtag(p, s, 5 * l + 1));
                 }
             }

@@ -125,6 +125,7 @@ cudaError_t launch_tile_rows(const __half* src, __half* dst, int rows, int cols,
                              cudaStream_t st);
 
 constexpr int kMaxStop = 32;
+constexpr int kMaxDecodeLayers = 64;  // layers the fused decode kernel takes (norm pointers in its parameters)
 constexpr int kDecodePartStride = 68;  // words per attention partial: m, l, 0, 0, o[64]
 
 struct DecodeParams {
@@ -136,7 +137,9 @@ struct DecodeParams {
     const __half* lm_head;  // tiled [vocab rounded up to 8][dim]
     const float* out_norm;
     const LayerW* layers;   // device array [n_layers]
+    const float* norm_w[2 * kMaxDecodeLayers];  // attn_norm of layer l at 2l, ffn_norm at 2l + 1
     RopeFreq rope;
+    const float2* rope_cs;  // [max_seq][head_dim / 2] (sin, cos) of pos * freq, rounded like RoPE.java:44-46
     // session buffers (device)
     float* kcache;  // [n_layers][n_kv][max_seq][head_dim]
     float* vcache;

@@ -42,6 +42,7 @@
 #include "lc_attention.cuh"
 #include "lc_internal.h"
 #include "lc_stream.cuh"
+#include "lc_tcgen05.cuh"
 
 #ifndef LC_DECODE_TRACE
 #error "define LC_DECODE_TRACE before including lc_decode_impl.cuh"
@@ -53,7 +54,7 @@ namespace {
 
 constexpr int kCW = 8;                // consumer warps
 constexpr int kCT = kCW * 32;         // consumer threads
-constexpr int kThreads = kCT + 128;   // + one warpgroup: the producer thread (warp kCW) and idle warps
+constexpr int kThreads = kCT + 128;   // + one warpgroup: producer (warp kCW), mover (warp kCW + 1), idle warps
 // Register split (setmaxnreg, per warpgroup): the launch gives every thread
 // 65536 / kThreads -> 168 registers; the producer warpgroup gives most of its
 // share to the consumer warpgroups.  The sum must stay within the launch
@@ -61,6 +62,7 @@ constexpr int kThreads = kCT + 128;   // + one warpgroup: the producer thread (w
 constexpr int kRegLaunch = 168, kRegConsumer = 224, kRegProducer = 56;
 static_assert(kCT * kRegConsumer + 128 * kRegProducer <= kThreads * kRegLaunch, "register split exceeds the pool");
 constexpr uint32_t kBarC = 1;         // named barrier of the consumer threads
+constexpr uint32_t kBarEnd = 6;       // consumers + the mover warp, before the TMEM is freed (2..5: attention pairs)
 constexpr int kBatchTiles = 8;        // tiles per epilogue batch
 constexpr int kMaxStages = 24;
 // Five 32 KB stages at dim 2048: the plan then fits the 196 KB shared-memory
@@ -71,6 +73,13 @@ constexpr int kRingBytes = 160 * 1024;
 constexpr int kAttnTmin = 64;         // positions per attention unit, at least
 constexpr int kAttnTmax = 384;        // ... and at most
 constexpr int kVChunk = 64;           // V positions staged in shared memory at a time
+// Tensor memory: the whole 512 columns as a ring of weight tiles.  A tile of
+// 8 rows x dim columns (dim = 128 KS) takes 4 KS columns of all 128 lanes.
+constexpr int kTmemCols = 512;
+constexpr int kTSlotsMax = 16;
+__host__ __device__ constexpr int tmem_slots(int KS) {
+    return kTmemCols / (4 * KS) < kTSlotsMax ? kTmemCols / (4 * KS) : kTSlotsMax;
+}
 
 enum Kind : int { kQKV = 0, kO = 1, kGU = 2, kDN = 3, kLM = 4 };
 
@@ -96,9 +105,9 @@ __host__ __device__ inline int attn_split_len(int seq, int G, int n_kv) {
 __host__ __device__ inline int attn_scratch_floats(int /*kv_mul*/) { return 2 * kVChunk * kAttnHeadDim; }
 
 struct Shared {
-    int stop;       // consumers -> producer: leave
+    int stop;       // consumers -> producer and mover: leave
     int next;       // argmax broadcast
-    float unscale;  // 2^-e of the staged GEMV input (see stage_split)
+    uint32_t tmem;  // TMEM base address (tcgen05.alloc)
     int pad;
     float red[kCW];
     float rmax[kCW];
@@ -122,8 +131,12 @@ __host__ __device__ constexpr Layout make_layout(int dim) {
                   0, 0, 0, 0};
 }
 
+// Barriers: full[kMaxStages], empty[kMaxStages] (smem stages), tfull,
+// tempty[kTSlotsMax] (TMEM slots), mdone.
+constexpr int kNumBars = 2 * kMaxStages + 2 * kTSlotsMax + 1;
+
 __host__ __device__ constexpr Layout finish_layout(Layout L) {
-    L.off_sh = L.off_bar + 2 * kMaxStages * 8;
+    L.off_sh = (L.off_bar + kNumBars * 8 + 15) / 16 * 16;  // act and ys take float4 accesses
     L.off_act = L.off_sh + (int)((sizeof(Shared) + 15) / 16 * 16);
     L.off_ys = L.off_act + kActFloats * 4;
     L.total = L.off_ys + kBatchTiles * 8 * kCW * 4;
@@ -133,14 +146,18 @@ __host__ __device__ constexpr Layout finish_layout(Layout L) {
 template <int KS>
 struct LayoutOf {
     static constexpr Layout L = finish_layout(make_layout(128 * KS));
+    static_assert((L.off_act & 15) == 0 && (L.off_ys & 15) == 0, "act and ys take float4 accesses");
 };
 
 struct Smem {
     uint8_t* ring;
-    uint64_t* full;
-    uint64_t* empty;
+    uint64_t* full;    // smem stage landed (TMA transaction bytes)
+    uint64_t* empty;   // smem stage copied to TMEM (mover's commit)
+    uint64_t* tfull;   // TMEM slot written (mover's commit)
+    uint64_t* tempty;  // TMEM slot read by every consumer warp
+    uint64_t* mdone;   // the mover's last copies finished
     Shared* sh;
-    float* act;   // GEMV input (normalised x, att, h); attention scratch
+    float* act;   // GEMV input (normalised x, att, h) in fp32; attention scratch
     float* ys;    // [tile][row][warp] partial dot products of one batch
     int stages, tile_bytes;
 };
@@ -282,6 +299,69 @@ __device__ __forceinline__ void run_producer(const DecodeParams& p, const Smem& 
     }
 }
 
+// --------------------------------------------------------------- mover --
+
+// The mover thread takes the CTA's tiles in the producer's order: once a
+// tile has landed in its shared-memory stage and the next TMEM slot has been
+// read by every consumer warp, it copies the tile into the slot with
+// tcgen05.cp (kCopies pieces of 128 lanes x 256 bits) and commits twice, so
+// the slot turns full for the consumers and the stage free for the producer
+// when the copies are done.  With the stages and the slots together, up to
+// stages + slots tiles are in flight or resident per SM while the consumers
+// wait for an exchange.  Bounded waits, as the producer's.
+template <int KS>
+__device__ __forceinline__ void run_mover(const DecodeParams& p, const Smem& sm) {
+    constexpr uint32_t kSlotCols = 4 * KS, kSlots = tmem_slots(KS), kCopies = KS / 2;
+    const int cta = blockIdx.x;
+    volatile int* err = p.err;
+    volatile int* stop = &sm.sh->stop;
+    const int nlay = p.sched_n[2 * cta], ntot = nlay + p.sched_n[2 * cta + 1];
+    const uint32_t nst = (uint32_t)sm.stages, tb = (uint32_t)sm.tile_bytes;
+    const uint32_t ring = smem_u32(sm.ring), tmem = sm.sh->tmem;
+    auto wait = [&](uint64_t* bar, uint32_t par, int code) -> bool {
+        if (mbar_try_wait(bar, par)) return true;
+        const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
+        for (uint32_t k = 1;; ++k) {
+            if (mbar_try_wait(bar, par)) return true;
+            if ((k & 63u) == 0u) {
+                if (*stop != 0 || *err != 0) return false;
+                if (globaltimer_ns() > deadline) {
+                    atomicCAS(const_cast<int*>(err), 0, code);
+                    return false;
+                }
+            }
+        }
+    };
+    uint32_t it = 0;
+    bool ok = true;
+    for (int s = 0; s < p.nsteps && ok; ++s) {
+        const int n = lm_needed(p, p.pos0 + s) ? ntot : nlay;
+        for (int i = 0; i < n; ++i, ++it) {
+            const uint32_t stage = it % nst, spar = (it / nst) & 1u;
+            const uint32_t slot = it % kSlots, tpar = ((it / kSlots) & 1u) ^ 1u;
+            if (!wait(&sm.full[stage], spar, kDevTimeoutFull) || !wait(&sm.tempty[slot], tpar, kDevTimeoutEmpty)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (uint32_t j = 0; j < kCopies; ++j)
+                tc_cp_128x256b(tmem + slot * kSlotCols + 8u * j, tc_desc_kmajor(ring + stage * tb + 4096u * j, 128, 256));
+            tc_commit(&sm.tfull[slot]);
+            tc_commit(&sm.empty[stage]);
+        }
+    }
+    // Every issued copy must be done before the TMEM is freed.
+    tc_commit(sm.mdone);
+    const uint64_t deadline = globaltimer_ns() + 200000000ull;
+    while (!mbar_try_wait(sm.mdone, 0)) {
+        if (globaltimer_ns() > deadline) {
+            atomicCAS(const_cast<int*>(err), 0, (int)kDevTimeoutDrain);
+            break;
+        }
+    }
+}
+
 // ------------------------------------------------------- consumer helpers --
 
 __device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -298,107 +378,93 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
-
-// x0, x1 (already scaled) -> packed f16 hi pair and lo pair; hi + lo = x to
-// 2^-22 relative (the subtraction is exact: hi is x rounded to 11 bits).
-__device__ __forceinline__ void split_pair(float x0, float x1, uint32_t& hi, uint32_t& lo) {
-    const __half2 h = __floats2half2_rn(x0, x1);
-    const float2 hf = __half22float2(h);
-    hi = h2_bits(h);
-    lo = h2_bits(__floats2half2_rn(x0 - hf.x, x1 - hf.y));
-}
-
-// The staged GEMV input in act, split once per CTA: element pair p is the
-// uint2 {hi(2p, 2p+1), lo(2p, 2p+1)} of f16 pairs with x * 2^e = hi + lo to
-// 2^-22 relative (the subtraction is exact: hi is x rounded to 11 bits).
-// One scale per vector (max |x| * 2^e in [2^14, 2^15)) keeps both parts in
-// range; 2^-e goes to sh->unscale.  The thread's values v[k] are the float4
-// at index idx[k] of the vector (idx < 0: none).  split_store takes the
-// vector's maximum |x| m (to within an ulp or two; the same in every thread)
-// and ends with a barrier.
+// The staged GEMV input in act, fp32: the thread's values v[k] are the
+// float4 at index idx[k] of the vector (idx < 0: none).  Ends with a barrier
+// that also makes `ok` (the thread's status so far) CTA-uniform.
 template <int NV>
-__device__ __forceinline__ void split_store(const Smem& sm, const float4 (&v)[NV], const int (&idx)[NV], float m) {
-    const int tid = threadIdx.x;
-    int e = 0;
-    if (m > 0.0f) {
-        e = 14 - (((__float_as_int(m) >> 23) & 0xff) - 127);
-        e = e < -126 ? -126 : (e > 126 ? 126 : e);
-    }
-    const float sc = __int_as_float((127 + e) << 23);
-    if (tid == 0) sm.sh->unscale = __int_as_float((127 - e) << 23);
-#pragma unroll
-    for (int k = 0; k < NV; ++k) {
-        if (idx[k] >= 0) {
-            uint4 o;
-            split_pair(v[k].x * sc, v[k].y * sc, o.x, o.y);
-            split_pair(v[k].z * sc, v[k].w * sc, o.z, o.w);
-            reinterpret_cast<uint4*>(sm.act)[idx[k]] = o;
-        }
-    }
-    named_bar_sync(kBarC, kCT);
-}
-
-// The maximum of the vector first (one reduction round), then split_store.
-// `ok` is the thread's status so far; returns the CTA-uniform AND of it.
-template <int NV>
-__device__ __forceinline__ bool stage_split(const Smem& sm, const float4 (&v)[NV], const int (&idx)[NV], bool ok) {
-    const int tid = threadIdx.x, warp = tid >> 5;
-    float m = 0.0f;
+__device__ __forceinline__ bool stage_store(const Smem& sm, const float4 (&v)[NV], const int (&idx)[NV], bool ok) {
 #pragma unroll
     for (int k = 0; k < NV; ++k)
-        if (idx[k] >= 0) m = fmaxf(m, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
-    m = warp_max(m);
-    if ((tid & 31) == 0) sm.sh->rmax[warp] = m;
-    ok = !bar_red_or(kBarC, kCT, !ok);
-#pragma unroll
-    for (int k = 0; k < kCW; ++k) m = fmaxf(m, sm.sh->rmax[k]);
-    split_store<NV>(sm, v, idx, m);
-    return ok;
+        if (idx[k] >= 0) reinterpret_cast<float4*>(sm.act)[idx[k]] = v[k];
+    return !bar_red_or(kBarC, kCT, !ok);
 }
 
-// A fragments of the warp's column slice (KS k-steps of 16 columns) of column
-// block cb of the split input: rows 0-7 of A carry hi, rows 8-15 lo, so
-// D[g][n] + D[g+8][n] is the dot product of weight row n with x * 2^e.
-template <int KS>
-__device__ __forceinline__ void build_frags(const Smem& sm, int col0, uint32_t (&af)[KS][4]) {
-    const int warp = threadIdx.x >> 5, t = threadIdx.x & 3;
-    const uint2* base = reinterpret_cast<const uint2*>(sm.act) + (col0 + warp * (KS * 16)) / 2 + t;
-#pragma unroll
-    for (int j = 0; j < KS; ++j) {
-        const uint2 a = base[8 * j], b = base[8 * j + 4];
-        af[j][0] = a.x;
-        af[j][1] = a.y;
-        af[j][2] = b.x;
-        af[j][3] = b.y;
-    }
-}
+// Weight tiles in tensor memory.  tcgen05.cp.128x256b of a tile's bytes
+// [4096 j, 4096 j + 4096) (column octets 32 j .. 32 j + 31 of the 8 rows,
+// tiled layout of lc_internal.h) under a K-major no-swizzle descriptor with
+// leading byte offset 128 and stride byte offset 256 puts row r, columns
+// 256 j + 16 m + 2 cc and +1 into TMEM lane 8 m + r, column 8 j + cc of the
+// tile's slot (m < 16, cc < 8).  Consumer warp w reads the lanes of its
+// quarter q = w % 4 (m = 4 q + lane / 8, row r = lane % 8) and the slot's
+// columns [2 KS h, 2 KS (h + 1)), h = w / 4: 2 KS words = 4 KS halves of one
+// row, whose input columns are fixed per thread -- the x segment below.
 
-// One tile: rows 2t, 2t+1 of the tile (valid in lanes t = 0..3) over the
-// warp's column slice.
+// Input column of half e (0, 1) of word k of the thread's share of a tile.
 template <int KS>
-__device__ __forceinline__ void mma_tile(uint32_t tile, const uint32_t (&af)[KS][4], float& y0, float& y1) {
-    constexpr int NS = KS < 4 ? KS : 4;  // independent accumulators
+__device__ __forceinline__ int xs_col(int k, int e) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t a = tile + warp * (KS * 256) + lane * 16;
-    uint32_t b[KS / 2][4];
+    const int m = 4 * (warp & 3) + (lane >> 3), c = 2 * KS * (warp >> 2) + k;
+    return 256 * (c >> 3) + 16 * m + 2 * (c & 7) + e;
+}
+
+// The thread's x segment of column block cb (4 KS floats) from act.
+template <int KS>
+__device__ __forceinline__ void build_xs(const Smem& sm, int col0, float (&xs)[4 * KS]) {
 #pragma unroll
-    for (int i = 0; i < KS / 2; ++i) ldsm4(a + i * 512, b[i][0], b[i][1], b[i][2], b[i][3]);
-    float d[NS][4];
-#pragma unroll
-    for (int s = 0; s < NS; ++s) d[s][0] = d[s][1] = d[s][2] = d[s][3] = 0.0f;
-#pragma unroll
-    for (int i = 0; i < KS / 2; ++i) {
-        mma16816(d[(2 * i) % NS], af[2 * i], b[i][0], b[i][1]);
-        mma16816(d[(2 * i + 1) % NS], af[2 * i + 1], b[i][2], b[i][3]);
+    for (int k = 0; k < 2 * KS; k += 2) {
+        const float4 v = *reinterpret_cast<const float4*>(sm.act + col0 + xs_col<KS>(k, 0));
+        xs[2 * k] = v.x;
+        xs[2 * k + 1] = v.y;
+        xs[2 * k + 2] = v.z;
+        xs[2 * k + 3] = v.w;
     }
-    y0 = d[0][0] + d[0][2];
-    y1 = d[0][1] + d[0][3];
-#pragma unroll
-    for (int s = 1; s < NS; ++s) {
-        y0 += d[s][0] + d[s][2];
-        y1 += d[s][1] + d[s][3];
+}
+
+// 2 KS consecutive 32-bit TMEM columns of the warp's 32 lanes (thread i:
+// lane base + i), waited for.
+template <int KS>
+__device__ __forceinline__ void tmem_ld_share(uint32_t taddr, uint32_t (&v)[2 * KS]) {
+    if constexpr (KS == 16) {
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+              "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]),
+              "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]),
+              "=r"(v[30]), "=r"(v[31])
+            : "r"(taddr));
+    } else if constexpr (KS == 8) {
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+            : "r"(taddr));
+    } else if constexpr (KS == 4) {
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                     : "r"(taddr));
+    } else {
+        static_assert(KS == 2, "dim 256, 512, 1024 or 2048");
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                     : "r"(taddr));
     }
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// The thread's partial dot product over its share of one tile: exact
+// products of the F16 weights with the fp32 inputs, four fp32 chains.
+template <int KS>
+__device__ __forceinline__ float dot_share(const uint32_t (&v)[2 * KS], const float (&xs)[4 * KS]) {
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k < 2 * KS; ++k) {
+        const float2 w = __half22float2(*reinterpret_cast<const __half2*>(&v[k]));
+        a[(2 * k) & 3] = fmaf(w.x, xs[2 * k], a[(2 * k) & 3]);
+        a[(2 * k + 1) & 3] = fmaf(w.y, xs[2 * k + 1], a[(2 * k + 1) & 3]);
+    }
+    return (a[0] + a[1]) + (a[2] + a[3]);
 }
 
 // Tag of exchange k (0..5L) of step s: QKV, ATT, O, GU, DN of layer l are
@@ -661,7 +727,7 @@ __device__ __forceinline__ bool stage_norm(const DecodeParams& p, const Smem& sm
             o[k].w = __fmul_rn(__fmul_rn(xv[k].w, inv), wv[k].w);
         }
     }
-    return stage_split<2>(sm, o, idx, ok);
+    return stage_store<2>(sm, o, idx, ok);
 }
 
 // Attention output of all heads -> act.  One split: copy; several: merge the
@@ -712,7 +778,7 @@ __device__ __forceinline__ bool stage_att(const DecodeParams& p, const Smem& sm,
         idx[1] = idx[0] + 1;
     }
     tr.mark();
-    return stage_split<2>(sm, v, idx, ok);
+    return stage_store<2>(sm, v, idx, ok);
 }
 
 // Sum over column blocks and warps of row r (0..7) of group gg of a batch of
@@ -831,6 +897,9 @@ __device__ __forceinline__ Smem smem_view() {
     sm.ring = smem_raw;
     sm.full = reinterpret_cast<uint64_t*>(smem_raw + L.off_bar);
     sm.empty = sm.full + kMaxStages;
+    sm.tfull = sm.empty + kMaxStages;
+    sm.tempty = sm.tfull + kTSlotsMax;
+    sm.mdone = sm.tempty + kTSlotsMax;
     sm.sh = reinterpret_cast<Shared*>(smem_raw + L.off_sh);
     sm.act = reinterpret_cast<float*>(smem_raw + L.off_act);
     sm.ys = reinterpret_cast<float*>(smem_raw + L.off_ys);
@@ -840,48 +909,51 @@ __device__ __forceinline__ Smem smem_view() {
 }
 
 struct RingPos {
-    uint32_t slot, par;         // next stage and its phase parity
-    int ok;                     // every stage so far was seen landing
-    unsigned long long waited;  // trace only: thread 0's ns waiting for stages
+    uint32_t slot, par;         // next TMEM slot and its phase parity
+    int ok;                     // every slot so far was seen written
+    unsigned long long waited;  // trace only: thread 0's ns waiting for slots
 };
 
-// The tiles of one batch (column blocks 0..ncb-1, groups [b0, b1)) into ys.
-// Out of line: the hot loop gets a register allocation of its own, with
-// nothing of the caller's state live in it.
+// The tiles of one batch (column blocks 0..ncb-1, groups [b0, b1)) into ys:
+// per tile, the warp waits for its TMEM slot, loads its share, releases the
+// slot at once (the mover may refill it while the products run), and lanes
+// r < 8 write the warp's partial sum of row r.
 template <int KS>
 __device__ __forceinline__ RingPos consume_batch(const DecodeParams& p, RingPos r, int b0, int b1, int ncb, bool timing) {
+    constexpr uint32_t kSlotCols = 4 * KS, kSlots = tmem_slots(KS);
     const Smem sm = smem_view<KS>();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, ng = b1 - b0;
-    const uint32_t ring = smem_u32(sm.ring);
-    const float unscale = sm.sh->unscale;
+    const uint32_t tbase = sm.sh->tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 2u * KS * (uint32_t)(warp >> 2);
     for (int cb = 0; cb < ncb; ++cb) {
-        uint32_t af[KS][4];
-        build_frags<KS>(sm, cb * p.dim, af);
+        float xs[4 * KS];
+        build_xs<KS>(sm, cb * p.dim, xs);
 #pragma unroll 1
         for (int g = b0; g < b1; ++g) {
             const unsigned long long t0 = timing ? globaltimer_ns() : 0ull;
-            bool got = r.ok && (mbar_try_wait(&sm.full[r.slot], r.par) ||
-                                mbar_wait_bounded(&sm.full[r.slot], r.par, p.err, globaltimer_ns() + p.timeout_ns,
+            bool got = r.ok && (mbar_try_wait(&sm.tfull[r.slot], r.par) ||
+                                mbar_wait_bounded(&sm.tfull[r.slot], r.par, p.err, globaltimer_ns() + p.timeout_ns,
                                                   kDevTimeoutFull));
-            // ldmatrix / mma are warp-collective: the whole warp takes the same
-            // branch.  A stage that was not seen landing is never released
-            // (the producer then stops on the error word).
+            // tcgen05.ld is warp-collective: the whole warp takes the same
+            // branch.  A slot that was not seen written is never released
+            // (the mover then stops on the error word).
             got = __all_sync(0xffffffffu, got);
             if (timing) r.waited += globaltimer_ns() - t0;
-            float y0 = 0.0f, y1 = 0.0f;
+            float y = 0.0f;
             if (got) {
-                mma_tile<KS>(ring + r.slot * (uint32_t)sm.tile_bytes, af, y0, y1);
+                uint32_t v[2 * KS];
+                tc_fence_after();
+                tmem_ld_share<KS>(tbase + r.slot * kSlotCols, v);
+                tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sm.empty[r.slot]);
+                if (lane == 0) mbar_arrive(&sm.tempty[r.slot]);
+                y = dot_share<KS>(v, xs);
             } else {
                 r.ok = 0;
             }
-            if (lane < 4) {
-                float* yo = sm.ys + ((cb * ng + (g - b0)) * 8 + 2 * lane) * kCW + warp;
-                yo[0] = y0 * unscale;
-                yo[kCW] = y1 * unscale;
-            }
-            if (++r.slot == (uint32_t)sm.stages) {
+            y += __shfl_xor_sync(0xffffffffu, y, 8);
+            y += __shfl_xor_sync(0xffffffffu, y, 16);
+            if (lane < 8) sm.ys[((cb * ng + (g - b0)) * 8 + lane) * kCW + warp] = y;
+            if (++r.slot == kSlots) {
                 r.slot = 0;
                 r.par ^= 1u;
             }
@@ -1174,7 +1246,7 @@ __device__ __forceinline__ bool stage_h(const DecodeParams& p, const Smem& sm, u
         if (idx[k] >= 0) v[k] = __ldcg(reinterpret_cast<const float4*>(p.h) + i);
     }
     tr.mark();
-    return stage_split<NV>(sm, v, idx, ok);
+    return stage_store<NV>(sm, v, idx, ok);
 }
 
 // lm_head epilogue: the CTA's argmax candidate (LlamaInference.argmax
@@ -1359,23 +1431,46 @@ template <int KS>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
     constexpr Layout L = LayoutOf<KS>::L;
     const Smem sm = smem_view<KS>();
+    const int warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) {
         for (int s = 0; s < L.stages; ++s) {
             mbar_init(&sm.full[s], 1);
-            mbar_init(&sm.empty[s], kCW);
+            mbar_init(&sm.empty[s], 1);
         }
+        for (int t = 0; t < tmem_slots(KS); ++t) {
+            mbar_init(&sm.tfull[t], 1);
+            mbar_init(&sm.tempty[t], kCW);
+        }
+        mbar_init(sm.mdone, 1);
         sm.sh->stop = 0;
         sm.sh->next = 0;
         fence_mbar_init();
     }
+    // One CTA per SM (all shared memory taken): the whole TMEM is free.
+    if (warp == kCW + 1) {
+        tmem_alloc(&sm.sh->tmem, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
     if (threadIdx.x >= kCT) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegProducer));
-        if (threadIdx.x < kCT + 32) run_producer(p, sm);
+        if (warp == kCW) {
+            run_producer(p, sm);
+        } else if (warp == kCW + 1) {
+            if ((threadIdx.x & 31) == 0) run_mover<KS>(p, sm);
+            __syncwarp();
+            named_bar_sync(kBarEnd, kCT + 32);
+            tc_fence_after();
+            tmem_dealloc(sm.sh->tmem, kTmemCols);
+        }
         return;
     }
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegConsumer));
     run_consumer<KS>(p, sm);
+    tc_fence_before();
+    named_bar_sync(kBarEnd, kCT + 32);
 }
 
 template <int KS>

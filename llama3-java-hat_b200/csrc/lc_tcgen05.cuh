@@ -87,6 +87,13 @@ LC_DEV void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t
         : "memory");
 }
 
+// 128 TMEM lanes x 256 bits (8 columns from taddr) from the shared-memory
+// matrix of descriptor `desc` (row r -> lane r); asynchronous, ordered with
+// the thread's other tcgen05 operations, tracked by tc_commit.
+LC_DEV void tc_cp_128x256b(uint32_t taddr, uint64_t desc) {
+    asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
+}
+
 // The mbarrier receives one arrival when every tcgen05 operation this thread
 // issued before has completed.
 LC_DEV void tc_commit(uint64_t* bar) {

@@ -13,12 +13,15 @@ quotient with a floor of 1e-6 * max|r| (so near-zero entries count in full),
 and the normwise error max|g - r| / max|r|; `parity_report` returns all
 three for tests that log them.
 End to end: logits max-abs <= 1e-2; greedy tokens identical wherever the
-oracle's top-2 logit margin exceeds 1e-2.
+oracle's top-2 logit margin exceeds 1e-2.  Long decodes (hundreds of
+positions through every layer) are gated end to end plus a normwise bound
+of 1e-4 on the logits, with the relative figures reported.
 """
 import numpy as np
 
 KERNEL_REL_TOL = 1e-3
 LOGITS_ABS_TOL = 1e-2
+NORMWISE_E2E_TOL = 1e-4  # end-to-end logits: max|g - r| / max|r|
 MARGIN = 1e-2
 GATE_FLOOR = 1e-2    # floor of the gated relative error, as a fraction of max|r|
 STRICT_FLOOR = 1e-6  # floor of the strict (reported) relative error

@@ -210,8 +210,20 @@ typedef struct lc_config {
     int32_t max_seq;    /* MAX_SEQ_LEN 2048          (:37) */
     float rope_theta;   /* 500000 (H/TransformerBlock.java:136) */
     float rms_eps;      /* 1e-5 (K/RMSNorm.java:22) */
-    int32_t reserved[6];
+    int32_t weight_mode; /* LC_WEIGHTS_F16 (0, default) or LC_WEIGHTS_F32 (1):
+                            H/WeightStorageMode.java, chosen per model as
+                            H/LlamaInference.java:58-62, 102-108 does */
+    int32_t reserved[5];
 } lc_config;
+
+/* Weight storage modes (H/WeightStorageMode.java).  F16 and F16_FAST differ
+ * only in the Java host's storage; on the GPU both keep the F16 weights
+ * (tiled for the fused decode kernel).  F32 keeps the projections and the
+ * embedding as fp32 (F16 tensors widened exactly, F32 tensors as given; twice
+ * the memory) and decodes with fp32-weight GEMVs (K/GEMV.java:34-43).  The
+ * multi-sequence batch (lc_batch_*) needs F16 weights. */
+#define LC_WEIGHTS_F16 0
+#define LC_WEIGHTS_F32 1
 
 typedef struct lc_model lc_model;
 
@@ -225,8 +237,11 @@ int lc_model_create(lc_context* ctx, const lc_config* cfg, lc_model** out);
 /* Uploads one tensor by its GGUF name ("token_embd.weight", "output.weight",
  * "output_norm.weight", "blk.N.attn_norm.weight", "blk.N.attn_q.weight", ...,
  * "blk.N.ffn_down.weight").  dtype: 0 = F32, 1 = F16 (raw half bits), the GGUF
- * type ids.  Projection weights must be F16, norms F32; n_elems must equal the
- * expected element count (LC_ERR_SHAPE otherwise, as H/LlamaModel.java:249-252). */
+ * type ids.  With LC_WEIGHTS_F16 projection weights must be F16
+ * (H/LlamaModel.java:238-240); with LC_WEIGHTS_F32 they may be F16 or F32
+ * (LlamaModel.mapTensor, :115-170).  Norms are F32 (F16 norms are widened);
+ * n_elems must equal the expected element count (LC_ERR_SHAPE otherwise, as
+ * H/LlamaModel.java:249-252). */
 int lc_model_upload_tensor(lc_model* m, const char* name, const void* data, int64_t n_elems, int32_t dtype);
 
 /* Checks that every tensor arrived (tied lm_head when "output.weight" is
@@ -237,6 +252,12 @@ int lc_model_finalize(lc_model* m);
  * validation) and uploads every tensor once; returns a finalized model.
  * max_seq <= 0 keeps the config default. */
 int lc_model_load_gguf(lc_context* ctx, const char* path, int32_t max_seq, lc_model** out);
+
+/* lc_model_load_gguf with a weight storage mode (LC_WEIGHTS_F16 or
+ * LC_WEIGHTS_F32): the LlamaInference(ggufPath, factory, backend, weightMode)
+ * constructor's choice, H/LlamaInference.java:58-62. */
+int lc_model_load_gguf_mode(lc_context* ctx, const char* path, int32_t max_seq, int32_t weight_mode,
+                            lc_model** out);
 
 int lc_model_get_config(const lc_model* m, lc_config* out);
 int lc_model_destroy(lc_model* m);

@@ -644,6 +644,12 @@ struct lc_model {
     float2* d_rope_cs = nullptr;  // [max_seq][head_dim / 2] (sin, cos) of the RoPE angles
     DecodeLaunch launch;
     int l2_prefetch_tiles = 0;    // producer L2 prefetch window (tiles)
+    // WeightStorageMode.F32: fp32 embedding and projections (row-major), the
+    // fused kernel's tiled F16 weights are not kept.
+    bool w32 = false;
+    float* tok32 = nullptr;       // [vocab][dim]
+    float* out32 = nullptr;       // output.weight, own allocation (tied: the embedding)
+    std::vector<F32Layer> l32;
     uint32_t* d_sched = nullptr;  // producer tile schedule (decode_build_schedule)
     int* d_sched_n = nullptr;
     int sched_stride = 0;
@@ -655,6 +661,11 @@ static int validate_config(const lc_config* c) {
         c->head_dim <= 0 || c->vocab <= 1 || c->max_seq <= 0)
         return fail(LC_ERR_INVALID_ARG, "config has a non-positive dimension");
     if (c->n_heads % c->n_kv_heads) return fail(LC_ERR_INVALID_ARG, "n_heads %% n_kv_heads != 0");
+    if (c->weight_mode != LC_WEIGHTS_F16 && c->weight_mode != LC_WEIGHTS_F32)
+        return fail(LC_ERR_INVALID_ARG, "Unknown weight storage mode %d (F16 = 0, F32 = 1)", c->weight_mode);
+    const char* why = nullptr;
+    if (c->weight_mode == LC_WEIGHTS_F32 && !f32_supported(c->dim, c->hidden, c->n_heads * c->head_dim, &why))
+        return fail(LC_ERR_UNSUPPORTED, "%s", why);
     return LC_OK;
 }
 
@@ -673,10 +684,14 @@ extern "C" int lc_model_create(lc_context* ctx, const lc_config* cfg, lc_model**
     const lc_config& c = *cfg;
     const size_t qdim = (size_t)c.n_heads * c.head_dim, kvd = (size_t)c.n_kv_heads * c.head_dim;
     auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
-    size_t per_layer = al((qdim + 2 * kvd) * c.dim * 2) + al((size_t)c.dim * qdim * 2) +
-                       al((size_t)2 * c.hidden * c.dim * 2) + al((size_t)c.dim * c.hidden * 2) + 2 * al((size_t)c.dim * 4);
+    // Bytes per projection / embedding element: F16, or fp32 in F32 mode.
+    const bool w32 = c.weight_mode == LC_WEIGHTS_F32;
+    const size_t eb = w32 ? 4 : 2;
+    m->w32 = w32;
+    size_t per_layer = al((qdim + 2 * kvd) * c.dim * eb) + al((size_t)c.dim * qdim * eb) +
+                       al((size_t)2 * c.hidden * c.dim * eb) + al((size_t)c.dim * c.hidden * eb) + 2 * al((size_t)c.dim * 4);
     const size_t vocab8 = ((size_t)c.vocab + 7) / 8 * 8;
-    size_t total = al((size_t)c.vocab * c.dim * 2) + al(vocab8 * c.dim * 2) + al((size_t)c.dim * 4) +
+    size_t total = al((size_t)c.vocab * c.dim * eb) + (w32 ? 0 : al(vocab8 * c.dim * 2)) + al((size_t)c.dim * 4) +
                    per_layer * c.n_layers;
     cudaError_t e = cudaMalloc(&m->arena, total);
     if (e != cudaSuccess) {
@@ -690,22 +705,39 @@ extern "C" int lc_model_create(lc_context* ctx, const lc_config* cfg, lc_model**
         p += al(b);
         return r;
     };
-    m->tok_emb = (__half*)take((size_t)c.vocab * c.dim * 2);
-    m->lm_tiled = (__half*)take(vocab8 * c.dim * 2);
-    m->out_norm = (float*)take((size_t)c.dim * 4);
     m->layers.resize(c.n_layers);
-    for (int l = 0; l < c.n_layers; ++l) {
-        LayerStore& L = m->layers[l];
-        L.wqkv = (__half*)take((qdim + 2 * kvd) * c.dim * 2);
-        L.wo = (__half*)take((size_t)c.dim * qdim * 2);
-        L.wgu = (__half*)take((size_t)2 * c.hidden * c.dim * 2);
-        L.wdown = (__half*)take((size_t)c.dim * c.hidden * 2);
-        L.attn_norm = (float*)take((size_t)c.dim * 4);
-        L.ffn_norm = (float*)take((size_t)c.dim * 4);
+    if (w32) {
+        m->tok32 = (float*)take((size_t)c.vocab * c.dim * 4);
+        m->out_norm = (float*)take((size_t)c.dim * 4);
+        m->l32.resize(c.n_layers);
+        for (int l = 0; l < c.n_layers; ++l) {
+            LayerStore& L = m->layers[l];
+            F32Layer& F = m->l32[l];
+            F.wqkv = (float*)take((qdim + 2 * kvd) * c.dim * 4);
+            F.wo = (float*)take((size_t)c.dim * qdim * 4);
+            F.wgu = (float*)take((size_t)2 * c.hidden * c.dim * 4);
+            F.wdown = (float*)take((size_t)c.dim * c.hidden * 4);
+            L.wqkv = L.wo = L.wgu = L.wdown = nullptr;
+            F.attn_norm = L.attn_norm = (float*)take((size_t)c.dim * 4);
+            F.ffn_norm = L.ffn_norm = (float*)take((size_t)c.dim * 4);
+        }
+    } else {
+        m->tok_emb = (__half*)take((size_t)c.vocab * c.dim * 2);
+        m->lm_tiled = (__half*)take(vocab8 * c.dim * 2);
+        m->out_norm = (float*)take((size_t)c.dim * 4);
+        for (int l = 0; l < c.n_layers; ++l) {
+            LayerStore& L = m->layers[l];
+            L.wqkv = (__half*)take((qdim + 2 * kvd) * c.dim * 2);
+            L.wo = (__half*)take((size_t)c.dim * qdim * 2);
+            L.wgu = (__half*)take((size_t)2 * c.hidden * c.dim * 2);
+            L.wdown = (__half*)take((size_t)c.dim * c.hidden * 2);
+            L.attn_norm = (float*)take((size_t)c.dim * 4);
+            L.ffn_norm = (float*)take((size_t)c.dim * 4);
+        }
     }
     m->have.assign(kLayerBase + kPerLayer * c.n_layers, 0);
     // Padding rows of the tiled lm_head must read as zeros.
-    e = cudaMemset(m->lm_tiled, 0, vocab8 * c.dim * 2);
+    e = w32 ? cudaSuccess : cudaMemset(m->lm_tiled, 0, vocab8 * c.dim * 2);
     if (e != cudaSuccess) {
         lc_model_destroy(m);
         return cuda_fail(e, "weight arena");
@@ -728,6 +760,7 @@ extern "C" int lc_model_destroy(lc_model* m) {
     if (m->d_layers) cudaFree(m->d_layers);
     if (m->d_sched) cudaFree(m->d_sched);
     if (m->d_sched_n) cudaFree(m->d_sched_n);
+    if (m->out32) cudaFree(m->out32);
     if (m->d_rope_cs) cudaFree(m->d_rope_cs);
     delete m;
     return LC_OK;
@@ -777,6 +810,28 @@ static int put_tiled(lc_model* m, __half* dst, const void* data, int rows, int c
     return LC_OK;
 }
 
+// F32 storage mode: n elements of a host or device F32 (dtype 0) or F16
+// (dtype 1, widened exactly like LlamaModel.mapTensor, H/LlamaModel.java:159-164)
+// tensor into dst.
+static int put32(lc_model* m, float* dst, const void* data, int64_t n, int dtype) {
+    cudaStream_t st = m->ctx->stream;
+    if (dtype == 0) {
+        CK(cudaMemcpyAsync(dst, data, (size_t)n * 4, cudaMemcpyDefault, st), "tensor upload");
+        return LC_OK;
+    }
+    const size_t bytes = (size_t)n * 2;
+    if (m->staging_bytes < bytes) {
+        if (m->staging) cudaFree(m->staging);
+        m->staging = nullptr;
+        m->staging_bytes = 0;
+        CK(cudaMalloc(&m->staging, bytes), "weight staging buffer");
+        m->staging_bytes = bytes;
+    }
+    CK(cudaMemcpyAsync(m->staging, data, bytes, cudaMemcpyDefault, st), "tensor upload");
+    CK(launch_f16_to_f32((const __half*)m->staging, dst, n, st), "F16 to F32");
+    return LC_OK;
+}
+
 static int upload_norm(float* dst, const void* data, int64_t n, int dtype, cudaStream_t st) {
     if (dtype == 0) return put(dst, data, (size_t)n * 4, st);
     // F16 norm weights are widened like LlamaModel.mapTensor (H/LlamaModel.java:159-164).
@@ -808,8 +863,17 @@ extern "C" int lc_model_upload_tensor(lc_model* m, const char* name, const void*
     };
     int rc;
     if (!strcmp(name, "token_embd.weight") || !strcmp(name, "output.weight")) {
-        if ((rc = need_f16()) || (rc = expect((int64_t)c.vocab * c.dim))) return rc;
         const bool out_w = name[0] == 'o';
+        if (m->w32) {
+            if ((rc = expect((int64_t)c.vocab * c.dim))) return rc;
+            if (out_w && !m->out32) CK(cudaMalloc(&m->out32, (size_t)n * 4), "output weight");
+            if ((rc = put32(m, out_w ? m->out32 : m->tok32, data, n, dtype))) return rc;
+            m->have[out_w ? kOutput : kTokEmb] = 1;
+            m->has_output |= out_w;
+            CK(cudaStreamSynchronize(st), "tensor upload");
+            return LC_OK;
+        }
+        if ((rc = need_f16()) || (rc = expect((int64_t)c.vocab * c.dim))) return rc;
         if (out_w) {
             if ((rc = put_tiled(m, m->lm_tiled, data, c.vocab, c.dim, 0, 1))) return rc;
         } else if ((rc = put(m->tok_emb, data, (size_t)n * 2, st))) {
@@ -836,23 +900,32 @@ extern "C" int lc_model_upload_tensor(lc_model* m, const char* name, const void*
             slot = kFfnNorm;
         } else if (!strcmp(t, "attn_q.weight") || !strcmp(t, "attn_k.weight") || !strcmp(t, "attn_v.weight")) {
             const int64_t rows = (t[5] == 'q') ? qdim : kvd;
-            if ((rc = need_f16()) || (rc = expect(rows * c.dim))) return rc;
+            if ((rc = (m->w32 ? 0 : need_f16())) || (rc = expect(rows * c.dim))) return rc;
             const int64_t row0 = (t[5] == 'q') ? 0 : (t[5] == 'k') ? qdim : qdim + kvd;
-            if ((rc = put_tiled(m, L.wqkv, data, (int)rows, c.dim, (int)row0, 1))) return rc;
+            if (m->w32) rc = put32(m, const_cast<float*>(m->l32[l].wqkv) + row0 * c.dim, data, n, dtype);
+            else rc = put_tiled(m, L.wqkv, data, (int)rows, c.dim, (int)row0, 1);
+            if (rc) return rc;
             slot = (t[5] == 'q') ? kQ : (t[5] == 'k') ? kK : kV;
         } else if (!strcmp(t, "attn_output.weight")) {
-            if ((rc = need_f16()) || (rc = expect((int64_t)c.dim * qdim))) return rc;
-            if ((rc = put_tiled(m, L.wo, data, c.dim, (int)qdim, 0, 1))) return rc;
+            if ((rc = (m->w32 ? 0 : need_f16())) || (rc = expect((int64_t)c.dim * qdim))) return rc;
+            if (m->w32) rc = put32(m, const_cast<float*>(m->l32[l].wo), data, n, dtype);
+            else rc = put_tiled(m, L.wo, data, c.dim, (int)qdim, 0, 1);
+            if (rc) return rc;
             slot = kO;
         } else if (!strcmp(t, "ffn_gate.weight") || !strcmp(t, "ffn_up.weight")) {
-            if ((rc = need_f16()) || (rc = expect((int64_t)c.hidden * c.dim))) return rc;
-            // Row r of gate -> row 2r of the packed matrix, row r of up -> 2r+1.
+            if ((rc = (m->w32 ? 0 : need_f16())) || (rc = expect((int64_t)c.hidden * c.dim))) return rc;
             const bool up = t[4] == 'u';
-            if ((rc = put_tiled(m, L.wgu, data, c.hidden, c.dim, up ? 1 : 0, 2))) return rc;
+            // F16: row r of gate -> row 2r of the packed tiled matrix, row r of
+            // up -> 2r+1.  F32: gate rows, then up rows.
+            if (m->w32) rc = put32(m, const_cast<float*>(m->l32[l].wgu) + (up ? (int64_t)c.hidden * c.dim : 0), data, n, dtype);
+            else rc = put_tiled(m, L.wgu, data, c.hidden, c.dim, up ? 1 : 0, 2);
+            if (rc) return rc;
             slot = up ? kUp : kGate;
         } else if (!strcmp(t, "ffn_down.weight")) {
-            if ((rc = need_f16()) || (rc = expect((int64_t)c.dim * c.hidden))) return rc;
-            if ((rc = put_tiled(m, L.wdown, data, c.dim, c.hidden, 0, 1))) return rc;
+            if ((rc = (m->w32 ? 0 : need_f16())) || (rc = expect((int64_t)c.dim * c.hidden))) return rc;
+            if (m->w32) rc = put32(m, const_cast<float*>(m->l32[l].wdown), data, n, dtype);
+            else rc = put_tiled(m, L.wdown, data, c.dim, c.hidden, 0, 1);
+            if (rc) return rc;
             slot = kDown;
         } else {
             return fail(LC_ERR_NOT_FOUND, "Tensor not found: %s", name);
@@ -918,6 +991,18 @@ extern "C" int lc_model_finalize(lc_model* m) {
     for (size_t s = 0; s < m->have.size(); ++s) {
         if (s == kOutput) continue;  // optional: tied embeddings
         if (!m->have[s]) return fail(LC_ERR_NOT_FOUND, "Tensor not found: %s", slot_name((int)s, buf));
+    }
+    if (m->w32) {
+        // Row-major fp32 weights as uploaded; nothing to tile or plan.
+        CK(cudaStreamSynchronize(m->ctx->stream), "weight upload");
+        if (m->staging) cudaFree(m->staging);
+        m->staging = nullptr;
+        m->staging_bytes = 0;
+        make_rope_freq(&m->rope, m->cfg.rope_theta, m->cfg.head_dim);
+        CK(f32_prepare(), "fp32 GEMV setup");
+        m->launch.grid = m->ctx->sms;
+        m->finalized = true;
+        return LC_OK;
     }
     // Tied embeddings: the lm_head is the token embedding (LlamaInference.java:69-72).
     if (!m->has_output) {
@@ -990,7 +1075,73 @@ struct lc_session {
     float last_ms = 0.0f;
     unsigned long long* trace = nullptr;  // phase trace buffer (debug), grid x trace_words
     int trace_words = 0;
+    void* f32mem = nullptr;  // F32 storage mode: the per-launch scratch of F32Step
+    F32Step f32;
 };
+
+// F32 storage mode: the session's F32Step (its caches, logits and tokens,
+// plus the fp32 path's scratch, position / length tables and attention
+// scratch sized for max_seq positions).
+static cudaError_t f32_session_setup(lc_session* s) {
+    lc_model* m = s->m;
+    const lc_config& c = m->cfg;
+    const size_t qd = (size_t)c.n_heads * c.head_dim, kvd = (size_t)c.n_kv_heads * c.head_dim;
+    // Splits hold at least 64 positions, so ceil(max_seq / 64) bounds every plan.
+    AttnPlan bound = plan_attention(1, c.n_heads, c.n_kv_heads, c.head_dim, c.max_seq, m->ctx->sms);
+    bound.max_splits = (c.max_seq + 63) / 64;
+    const size_t att_bytes = attention_scratch_bytes(bound);
+    auto al = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    const size_t sizes[] = {(size_t)c.dim * 4, (size_t)c.dim * 4, (qd + 2 * kvd) * 4, qd * 4, (size_t)c.hidden * 8,
+                            (size_t)c.max_seq * 4, (size_t)c.max_seq * 4, att_bytes};
+    size_t total = 0;
+    for (size_t x : sizes) total += al(x);
+    cudaError_t e = cudaMalloc(&s->f32mem, total);
+    if (e != cudaSuccess) return e;
+    uint8_t* p = (uint8_t*)s->f32mem;
+    void* ptr[8];
+    for (int i = 0; i < 8; ++i) {
+        ptr[i] = p;
+        p += al(sizes[i]);
+    }
+    std::vector<int32_t> pv(c.max_seq), lv(c.max_seq);
+    for (int i = 0; i < c.max_seq; ++i) {
+        pv[i] = i;
+        lv[i] = i + 1;
+    }
+    if ((e = cudaMemcpy(ptr[5], pv.data(), pv.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess) return e;
+    if ((e = cudaMemcpy(ptr[6], lv.data(), lv.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess) return e;
+    F32Step& f = s->f32;
+    f.dim = c.dim;
+    f.hidden = c.hidden;
+    f.n_layers = c.n_layers;
+    f.n_heads = c.n_heads;
+    f.n_kv = c.n_kv_heads;
+    f.head_dim = c.head_dim;
+    f.vocab = c.vocab;
+    f.max_seq = c.max_seq;
+    f.num_sms = m->ctx->sms;
+    f.eps = c.rms_eps;
+    f.tok_emb = m->tok32;
+    f.lm = m->has_output ? m->out32 : m->tok32;  // tied embeddings, LlamaInference.java:69-72
+    f.out_norm = m->out_norm;
+    f.layers = m->l32.data();
+    f.rope = m->rope;
+    f.kcache = s->kcache;
+    f.vcache = s->vcache;
+    f.logits = s->logits;
+    f.tokens = s->tokens;
+    f.err = s->err;
+    f.x = (float*)ptr[0];
+    f.xb = (float*)ptr[1];
+    f.qkv = (float*)ptr[2];
+    f.att = (float*)ptr[3];
+    f.gu = (float*)ptr[4];
+    f.posv = (const int32_t*)ptr[5];
+    f.lenv = (const int32_t*)ptr[6];
+    f.attn_scratch = ptr[7];
+    f.attn_scratch_bytes = att_bytes;
+    return cudaSuccess;
+}
 
 extern "C" int lc_session_create(lc_model* m, lc_session** out) {
     if (!m || !out) return fail(LC_ERR_INVALID_ARG, "NULL argument");
@@ -1057,6 +1208,7 @@ extern "C" int lc_session_create(lc_model* m, lc_session** out) {
     if (e == cudaSuccess) e = cudaHostGetDevicePointer((void**)&s->stream_dev, s->stream_host, 0);
     if (e == cudaSuccess) e = cudaEventCreate(&s->ev0);
     if (e == cudaSuccess) e = cudaEventCreate(&s->ev1);
+    if (e == cudaSuccess && m->w32) e = f32_session_setup(s);
     if (e != cudaSuccess) {
         lc_session_destroy(s);
         return cuda_fail(e, "session setup");
@@ -1075,6 +1227,7 @@ extern "C" int lc_session_destroy(lc_session* s) {
     if (s->ev0) cudaEventDestroy(s->ev0);
     if (s->ev1) cudaEventDestroy(s->ev1);
     if (s->trace) cudaFree(s->trace);
+    if (s->f32mem) cudaFree(s->f32mem);
     delete s;
     return LC_OK;
 }
@@ -1088,8 +1241,50 @@ struct TokenSink {
 // Launches the fused kernel for positions pos0..pos0+nsteps-1 and waits.  With
 // a sink, the kernel publishes each generated token to the session's mapped
 // stream buffer and this thread hands them to the callback while it waits.
+// F32 storage mode: the same contract as the fused launch below, one
+// enqueued forward per position.  Position pos feeds tokens[pos] (the prompt,
+// or the greedy token the previous position stored); logits are computed when
+// needed (not for prompt positions under skip_prefill_logits) and the argmax
+// goes to tokens[pos + 1] from the last prompt position on.  With stop tokens
+// or a sink the generated token is read back after each position.
+static int run_steps_f32(lc_session* s, int pos0, int nsteps, int n_prompt, int skip_prefill_logits,
+                         const int32_t* stop, int n_stop, int* n_done, const TokenSink* sink) {
+    lc_model* m = s->m;
+    cudaStream_t st = m->ctx->stream;
+    CK(cudaMemsetAsync(s->err, 0, sizeof(int), st), "clear error word");
+    CK(cudaEventRecord(s->ev0, st), "event");
+    int done = 0;
+    for (int k = 0; k < nsteps; ++k) {
+        const int pos = pos0 + k;
+        const bool lm = !(skip_prefill_logits && pos + 1 < n_prompt);
+        const bool store = lm && pos + 1 >= n_prompt;
+        CK(f32_forward(s->f32, pos, lm, store, st), "fp32-weight forward");
+        done = k + 1;
+        if (store && (n_stop > 0 || sink)) {
+            CK(cudaMemcpyAsync(s->pinned + 3, s->tokens + pos + 1, 4, cudaMemcpyDeviceToHost, st), "token read");
+            CK(cudaStreamSynchronize(st), "fp32-weight forward");
+            const int tok = s->pinned[3];
+            if (sink) sink->cb(tok, pos + 1 - n_prompt, sink->user);
+            bool stop_now = false;
+            for (int j = 0; j < n_stop; ++j) stop_now |= stop[j] == tok;
+            if (stop_now) break;
+        }
+    }
+    CK(cudaEventRecord(s->ev1, st), "event");
+    CK(cudaMemcpyAsync(s->pinned, s->err, 4, cudaMemcpyDeviceToHost, st), "read error word");
+    CK(cudaStreamSynchronize(st), "fp32-weight forward");
+    cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1);
+    if (s->pinned[0] != 0) {
+        if (s->pinned[0] == kDevBadToken) return fail(LC_ERR_INVALID_ARG, "token id outside [0, %d)", m->cfg.vocab);
+        return fail(LC_ERR_TIMEOUT, "fp32-weight forward: device error code %d", s->pinned[0]);
+    }
+    *n_done = done;
+    return LC_OK;
+}
+
 static int run_steps(lc_session* s, int pos0, int nsteps, int n_prompt, int skip_prefill_logits,
                      const int32_t* stop, int n_stop, int* n_done, const TokenSink* sink = nullptr) {
+    if (s->m->w32) return run_steps_f32(s, pos0, nsteps, n_prompt, skip_prefill_logits, stop, n_stop, n_done, sink);
     lc_model* m = s->m;
     cudaStream_t st = m->ctx->stream;
     DecodeParams p;
@@ -1248,6 +1443,7 @@ extern "C" int lc_decode(lc_session* s, int32_t token, int32_t start_pos, int32_
 extern "C" int lc_session_enable_trace(lc_session* s, int32_t words_per_cta) {
     if (!s || words_per_cta < 0) return fail(LC_ERR_INVALID_ARG, "bad argument");
     CTX_CHECK(s->m->ctx);
+    if (s->m->w32) return fail(LC_ERR_UNSUPPORTED, "the phase trace belongs to the fused F16 decode kernel");
     CK(cudaStreamSynchronize(s->m->ctx->stream), "synchronize");
     if (s->trace) cudaFree(s->trace);
     s->trace = nullptr;
@@ -1288,6 +1484,7 @@ extern "C" int lc_batch_create(lc_model* m, int32_t max_batch, lc_batch** out) {
     if (!m || !out) return fail(LC_ERR_INVALID_ARG, "NULL argument");
     CTX_CHECK(m->ctx);
     if (!m->finalized) return fail(LC_ERR_STATE, "model not finalized");
+    if (m->w32) return fail(LC_ERR_UNSUPPORTED, "multi-sequence batches run on F16 weights (LC_WEIGHTS_F16)");
     if (max_batch < 1 || max_batch > kGemmMaxB) return fail(LC_ERR_INVALID_ARG, "max_batch %d not in 1..%d", max_batch, kGemmMaxB);
     BatchModel bm;
     const lc_config& c = m->cfg;

@@ -124,7 +124,14 @@ struct TensorInfo {
 }  // namespace
 
 extern "C" int lc_model_load_gguf(lc_context* ctx, const char* path, int32_t max_seq, lc_model** out) {
+    return lc_model_load_gguf_mode(ctx, path, max_seq, LC_WEIGHTS_F16, out);
+}
+
+extern "C" int lc_model_load_gguf_mode(lc_context* ctx, const char* path, int32_t max_seq, int32_t weight_mode,
+                                       lc_model** out) {
     if (!ctx || !path || !out) return lc_gguf_set_error(LC_ERR_INVALID_ARG, "NULL argument");
+    if (weight_mode != LC_WEIGHTS_F16 && weight_mode != LC_WEIGHTS_F32)
+        return lc_gguf_set_error(LC_ERR_INVALID_ARG, "Unknown weight storage mode (F16 = 0, F32 = 1)");
     int fd = open(path, O_RDONLY);
     if (fd < 0) return lc_gguf_set_error(LC_ERR_IO, "cannot open GGUF file");
     struct stat st;
@@ -209,6 +216,7 @@ extern "C" int lc_model_load_gguf(lc_context* ctx, const char* path, int32_t max
         }
         if (cfg.dim > 0) cfg.vocab = (int32_t)(emb->second.elems() / (uint64_t)cfg.dim);
         if (max_seq > 0) cfg.max_seq = max_seq;
+        cfg.weight_mode = weight_mode;
         if ((rc = lc_model_create(ctx, &cfg, &m)) != LC_OK) break;
         for (auto& kv : tensors) {
             const TensorInfo& ti = kv.second;

@@ -76,6 +76,41 @@ cudaError_t launch_ex(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, 
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
 }
 
+// ---- decode with fp32 weights, WeightStorageMode.F32 (lc_f32.cu) ----
+struct F32Layer {
+    const float* wqkv;   // [n_heads*head_dim + 2*kv_dim][dim]: q rows, then k, then v
+    const float* wo;     // [dim][n_heads*head_dim]
+    const float* wgu;    // [2*hidden][dim]: gate rows, then up rows
+    const float* wdown;  // [dim][hidden]
+    const float* attn_norm;
+    const float* ffn_norm;
+};
+// Everything one fp32-weight forward touches (device pointers; `layers` is a
+// host array).
+struct F32Step {
+    int dim, hidden, n_layers, n_heads, n_kv, head_dim, vocab, max_seq, num_sms;
+    float eps;
+    const float* tok_emb;   // [vocab][dim]
+    const float* lm;        // [vocab][dim]: output.weight or the tied embedding
+    const float* out_norm;
+    const F32Layer* layers;
+    RopeFreq rope;
+    float *kcache, *vcache, *logits;  // the session's ([n_layers][n_kv][max_seq][head_dim] caches)
+    int32_t* tokens;                  // token fed at each position; the argmax goes to tokens[pos + 1]
+    int* err;
+    float *x, *xb, *qkv, *att, *gu;   // scratch: dim, dim, q+k+v, n_heads*head_dim, 2*hidden
+    const int32_t* posv;              // posv[i] = i
+    const int32_t* lenv;              // lenv[i] = i + 1
+    void* attn_scratch;
+    size_t attn_scratch_bytes;
+};
+cudaError_t launch_f16_to_f32(const __half* src, float* dst, long long n, cudaStream_t st);
+bool f32_supported(int dim, int hidden, int qdim, const char** why);
+cudaError_t f32_prepare();
+// Enqueues one forward at `pos` (token tokens[pos]); with `logits` the final
+// norm, lm_head and, with `store_token`, the argmax into tokens[pos + 1].
+cudaError_t f32_forward(const F32Step& f, int pos, bool logits, bool store_token, cudaStream_t st);
+
 // ---- argmax-key all-reduce over peer memory (lc_keyx.cu) ----
 constexpr int kKeyxMaxWorld = 8;
 struct KeyxArgs {

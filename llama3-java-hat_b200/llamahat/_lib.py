@@ -62,7 +62,7 @@ class LcConfig(ctypes.Structure):
     _fields_ = [
         ("dim", c_int32), ("hidden", c_int32), ("n_layers", c_int32), ("n_heads", c_int32),
         ("n_kv_heads", c_int32), ("head_dim", c_int32), ("vocab", c_int32), ("max_seq", c_int32),
-        ("rope_theta", c_float), ("rms_eps", c_float), ("reserved", c_int32 * 6),
+        ("rope_theta", c_float), ("rms_eps", c_float), ("weight_mode", c_int32), ("reserved", c_int32 * 5),
     ]
 
 
@@ -114,6 +114,7 @@ SIGNATURES = {
     "lc_model_upload_tensor": (c_int, [c_void_p, c_char_p, c_void_p, c_int64, c_int32]),
     "lc_model_finalize": (c_int, [c_void_p]),
     "lc_model_load_gguf": (c_int, [c_void_p, c_char_p, c_int32, POINTER(c_void_p)]),
+    "lc_model_load_gguf_mode": (c_int, [c_void_p, c_char_p, c_int32, c_int32, POINTER(c_void_p)]),
     "lc_model_get_config": (c_int, [c_void_p, POINTER(LcConfig)]),
     "lc_model_destroy": (c_int, [c_void_p]),
     "lc_session_create": (c_int, [c_void_p, POINTER(c_void_p)]),

@@ -6,6 +6,7 @@ rope theta TransformerBlock.java:136, eps kernels/RMSNorm.java:22).
 """
 from __future__ import annotations
 
+import enum
 from dataclasses import dataclass, replace
 
 from ._lib import LcConfig
@@ -57,3 +58,31 @@ LLAMA_3_2_1B = LlamaConfig()
 
 # Small configuration with the same structure (GQA 4:1, head_dim 64) for fast tests.
 TINY = LlamaConfig(dim=512, hidden=1024, n_layers=2, n_heads=8, n_kv_heads=2, head_dim=64, vocab=1000, max_seq=256)
+
+
+class WeightStorageMode(enum.Enum):
+    """How the projection weights are stored (H/WeightStorageMode.java).
+
+    F16 and F16_FAST differ only in the Java host's storage; on the GPU both
+    keep the F16 weights (tiled for the fused decode kernel).  F32 keeps the
+    projections and the embedding in fp32 (twice the memory) and decodes with
+    fp32-weight GEMVs.  The value is the C ABI's weight_mode."""
+    F32 = 1
+    F16 = 0
+    F16_FAST = 2
+
+    @property
+    def device_mode(self) -> int:
+        return 1 if self is WeightStorageMode.F32 else 0
+
+    @staticmethod
+    def fromString(s: str) -> "WeightStorageMode":
+        """WeightStorageMode.fromString (H/WeightStorageMode.java:63-70)."""
+        key = s.strip().upper()
+        if key == "F32":
+            return WeightStorageMode.F32
+        if key == "F16":
+            return WeightStorageMode.F16
+        if key in ("F16_FAST", "F16FAST", "FAST"):
+            return WeightStorageMode.F16_FAST
+        raise ValueError(f"Unknown weight storage mode: '{s}'. Valid: F16, F16_FAST, F32")

@@ -2,7 +2,9 @@
 
 The writer produces files the reference's loader accepts
 (GGUFReader.java:57-123, LlamaModel.java:74-86): general.architecture =
-"llama", F16 projection tensors, F32 norm tensors, tied embeddings (no
+"llama", F16 projection tensors (F32 when the arrays given are fp32, as
+LlamaModel.mapTensor reads them in WeightStorageMode.F32), F32 norm tensors,
+tied embeddings (no
 output.weight), 32-byte alignment, and -- when the vocabulary is the full
 128256 ids -- the tokenizer metadata LlamaInference's constructor reads
 (Tokenizer.java:47-95, ChatFormat.java:22-29): a gpt2 tokenizer model,
@@ -106,7 +108,8 @@ def write_gguf(path: str, cfg: LlamaConfig, weights: dict[str, np.ndarray], alig
         _s(info, name)
         dims = tuple(reversed(shape))  # GGUF lists ne0 (innermost) first
         info += struct.pack("<I", len(dims)) + b"".join(struct.pack("<Q", d) for d in dims)
-        info += struct.pack("<I", 1 if kind == "proj" else 0) + struct.pack("<Q", off)
+        ttype = 1 if a.dtype == np.float16 else 0  # GGML F16 or F32, as given
+        info += struct.pack("<I", ttype) + struct.pack("<Q", off)
         offsets.append(off)
         off += (nbytes + alignment - 1) // alignment * alignment
 
@@ -124,9 +127,9 @@ def write_gguf(path: str, cfg: LlamaConfig, weights: dict[str, np.ndarray], alig
                 f.write(b"\0" * (o - pos))
                 pos = o
             a = np.ascontiguousarray(weights[name])
-            want = np.float16 if kind == "proj" else np.float32
-            if a.dtype != want:
-                raise TypeError(f"{name}: expected {want}, got {a.dtype}")
+            want = (np.float16, np.float32) if kind == "proj" else (np.float32,)
+            if a.dtype not in want:
+                raise TypeError(f"{name}: expected {' or '.join(np.dtype(t).name for t in want)}, got {a.dtype}")
             f.write(a.tobytes())
             pos += a.nbytes
 

@@ -17,7 +17,7 @@ import weakref
 import numpy as np
 
 from . import _lib
-from .config import LlamaConfig
+from .config import LlamaConfig, WeightStorageMode
 from .kernels import Accelerator, _addr, default_accelerator
 
 EOS_TOKEN = 128001  # LlamaInference.java:174
@@ -27,12 +27,15 @@ class CudaModel:
     """Weights in HBM (one arena) plus the prepared decode kernel."""
 
     def __init__(self, cfg: LlamaConfig | None = None, weights: dict | None = None, gguf_path: str | None = None,
-                 acc: Accelerator | None = None, max_seq: int = 0):
+                 acc: Accelerator | None = None, max_seq: int = 0,
+                 weight_mode: WeightStorageMode = WeightStorageMode.F16):
         self.acc = acc or default_accelerator()
+        self.weight_mode = weight_mode
         lib = _lib.load()
         h = ctypes.c_void_p()
         if gguf_path is not None:
-            _lib.check(lib.lc_model_load_gguf(self.acc.handle, gguf_path.encode(), max_seq, ctypes.byref(h)))
+            _lib.check(lib.lc_model_load_gguf_mode(self.acc.handle, gguf_path.encode(), max_seq,
+                                                   weight_mode.device_mode, ctypes.byref(h)))
             c = _lib.LcConfig()
             _lib.check(lib.lc_model_get_config(h, ctypes.byref(c)))
             self.cfg = LlamaConfig.from_lc(c)
@@ -41,6 +44,7 @@ class CudaModel:
                 raise ValueError("need cfg and weights, or gguf_path")
             self.cfg = cfg
             lc = cfg.to_lc()
+            lc.weight_mode = weight_mode.device_mode
             _lib.check(lib.lc_model_create(self.acc.handle, ctypes.byref(lc), ctypes.byref(h)))
         self.handle = h
         self.gguf_path = gguf_path
@@ -201,7 +205,7 @@ class LlamaInference:
     chat() raises IllegalStateError."""
 
     def __init__(self, model: CudaModel | str, acc: Accelerator | None = None, max_seq: int = 0,
-                 tokenizer=None):
+                 tokenizer=None, weightMode: WeightStorageMode = WeightStorageMode.F16):
         from .tokenizer import ChatFormat, Tokenizer
         path = model if isinstance(model, str) else getattr(model, "gguf_path", None)
         if tokenizer is None and path is not None:
@@ -209,7 +213,8 @@ class LlamaInference:
             meta, _ = read_gguf(path)
             if isinstance(model, str) or meta.get("tokenizer.ggml.model") is not None:
                 tokenizer = Tokenizer.fromGGUFMetadata(meta)
-        self.model = model if isinstance(model, CudaModel) else CudaModel(gguf_path=model, acc=acc, max_seq=max_seq)
+        self.model = model if isinstance(model, CudaModel) else CudaModel(gguf_path=model, acc=acc, max_seq=max_seq,
+                                                                          weight_mode=weightMode)
         self.session = Session(self.model)
         self.cfg = self.model.cfg
         self.tokenizer = tokenizer

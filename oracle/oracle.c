@@ -290,7 +290,18 @@ typedef struct {
     const uint16_t* wgate[OR_MAX_LAYERS];
     const uint16_t* wup[OR_MAX_LAYERS];
     const uint16_t* wdown[OR_MAX_LAYERS];
+    /* WeightStorageMode.F32 (H/WeightStorageMode.java, LlamaInference.java:102-108):
+     * when set, tok_emb, out_w and the seven projections point to fp32 data
+     * (cast), multiplied by GEMV.apply(F32Array, ...) kernels/GEMV.java:34-43 and
+     * embedded by the F32Array case of LlamaInference.java:133-137. */
+    int f32;
 } or_model;
+
+/* The projection GEMV of the model's storage mode (TransformerBlock.java:219-226). */
+static void or_gemv_w(const or_model* m, const uint16_t* W, const float* x, float* y, int rows, int cols) {
+    if (m->f32) or_gemv_f32((const float*)(const void*)W, x, y, rows, cols);
+    else or_gemv_f16(W, x, y, rows, cols);
+}
 
 /* Per-sequence state: the fp32 KV caches LlamaInference allocates
  * (LlamaInference.java:83-89) plus the block scratch buffers
@@ -349,22 +360,22 @@ void or_block_forward(const or_model* m, int l, or_state* s, int pos) {
 
     memcpy(s->resid, s->x, (size_t)dim * 4);                         /* :139 */
     or_rmsnorm_eps(s->x, m->attn_norm[l], dim, m->rms_eps);          /* :142 */
-    or_gemv_f16(m->wq[l], s->x, s->q, nh * hd, dim);                 /* :145 */
-    or_gemv_f16(m->wk[l], s->x, s->k, kv_dim, dim);                  /* :146 */
-    or_gemv_f16(m->wv[l], s->x, s->v, kv_dim, dim);                  /* :147 */
+    or_gemv_w(m, m->wq[l], s->x, s->q, nh * hd, dim);                 /* :145 */
+    or_gemv_w(m, m->wk[l], s->x, s->k, kv_dim, dim);                  /* :146 */
+    or_gemv_w(m, m->wv[l], s->x, s->v, kv_dim, dim);                  /* :147 */
     or_rope(s->q, pos, nh, hd, m->rope_theta);                       /* :150 */
     or_rope(s->k, pos, nkv, hd, m->rope_theta);                      /* :151 */
     memcpy(kc + (size_t)pos * kv_dim, s->k, (size_t)kv_dim * 4);    /* :158-162 */
     memcpy(vc + (size_t)pos * kv_dim, s->v, (size_t)kv_dim * 4);
     or_gqa_attention(s->q, kc, vc, s->att, pos + 1, nh, nkv, hd, s->scores); /* :164-192 */
-    or_gemv_f16(m->wo[l], s->att, s->x, dim, nh * hd);               /* :195 */
+    or_gemv_w(m, m->wo[l], s->att, s->x, dim, nh * hd);               /* :195 */
     for (int i = 0; i < dim; ++i) s->x[i] = s->x[i] + s->resid[i];   /* :198, add() :234-238 */
     memcpy(s->resid, s->x, (size_t)dim * 4);                         /* :201 */
     or_rmsnorm_eps(s->x, m->ffn_norm[l], dim, m->rms_eps);           /* :204 */
-    or_gemv_f16(m->wgate[l], s->x, s->g, hidden, dim);               /* :207 */
-    or_gemv_f16(m->wup[l], s->x, s->u, hidden, dim);                 /* :208 */
+    or_gemv_w(m, m->wgate[l], s->x, s->g, hidden, dim);               /* :207 */
+    or_gemv_w(m, m->wup[l], s->x, s->u, hidden, dim);                 /* :208 */
     or_swiglu(s->g, s->u, hidden);                                   /* :209-210 */
-    or_gemv_f16(m->wdown[l], s->g, s->f, dim, hidden);               /* :211 */
+    or_gemv_w(m, m->wdown[l], s->g, s->f, dim, hidden);               /* :211 */
     for (int i = 0; i < dim; ++i) s->x[i] = s->resid[i] + s->f[i];   /* :214-216 */
 }
 
@@ -372,11 +383,16 @@ void or_block_forward(const or_model* m, int l, or_state* s, int pos) {
  * left in s->logits and copied to `logits_out` when it is not NULL. */
 void or_forward(const or_model* m, or_state* s, int token, int pos, float* logits_out) {
     f16_table_init();
-    const uint16_t* e = m->tok_emb + (size_t)token * (size_t)m->dim;
-    for (int i = 0; i < m->dim; ++i) s->x[i] = g_f16_table[e[i]];    /* :122-140 */
+    if (m->f32) {
+        const float* e = (const float*)(const void*)m->tok_emb + (size_t)token * (size_t)m->dim;
+        for (int i = 0; i < m->dim; ++i) s->x[i] = e[i];               /* :133-137 */
+    } else {
+        const uint16_t* e = m->tok_emb + (size_t)token * (size_t)m->dim;
+        for (int i = 0; i < m->dim; ++i) s->x[i] = g_f16_table[e[i]];    /* :122-132 */
+    }
     for (int l = 0; l < m->n_layers; ++l) or_block_forward(m, l, s, pos); /* :143-145 */
     or_rmsnorm_eps(s->x, m->out_norm, m->dim, m->rms_eps);           /* :148 */
-    or_gemv_f16(m->out_w, s->x, s->logits, m->vocab, m->dim);         /* :151-156 */
+    or_gemv_w(m, m->out_w, s->x, s->logits, m->vocab, m->dim);         /* :151-156 */
     if (logits_out) memcpy(logits_out, s->logits, (size_t)m->vocab * 4); /* :159-162 */
 }
 

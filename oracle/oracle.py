@@ -33,6 +33,7 @@ class _Model(ctypes.Structure):
         ("attn_norm", c_void_p * MAX_LAYERS), ("wq", c_void_p * MAX_LAYERS), ("wk", c_void_p * MAX_LAYERS),
         ("wv", c_void_p * MAX_LAYERS), ("wo", c_void_p * MAX_LAYERS), ("ffn_norm", c_void_p * MAX_LAYERS),
         ("wgate", c_void_p * MAX_LAYERS), ("wup", c_void_p * MAX_LAYERS), ("wdown", c_void_p * MAX_LAYERS),
+        ("f32", c_int),
     ]
 
 
@@ -197,9 +198,13 @@ def f16_to_f32(bits: int) -> float:
 # ----------------------------------------------------------------- model
 
 class OracleModel:
-    """LlamaInference with PlainJavaKernelFactory, restated in C (host memory)."""
+    """LlamaInference with PlainJavaKernelFactory, restated in C (host memory).
 
-    def __init__(self, cfg, weights: dict[str, np.ndarray]):
+    f32=True is WeightStorageMode.F32 (H/LlamaInference.java:102-108): the
+    embedding and the projections are fp32 (F16 tensors widened exactly, F32
+    tensors as given) and go through GEMV.apply(F32Array, ...)."""
+
+    def __init__(self, cfg, weights: dict[str, np.ndarray], f32: bool = False):
         if cfg.n_layers > MAX_LAYERS:
             raise ValueError("too many layers")
         self.cfg = cfg
@@ -207,7 +212,12 @@ class OracleModel:
 
         def ptr(name, dtype):
             a = weights[name]
-            a = f16_bits(a) if dtype == np.uint16 else np.ascontiguousarray(a, np.float32)
+            if dtype == np.uint16 and f32:
+                a = np.ascontiguousarray(a.astype(np.float32) if a.dtype == np.float16 else a, np.float32)
+            elif dtype == np.uint16:
+                a = f16_bits(a)
+            else:
+                a = np.ascontiguousarray(a, np.float32)
             self._keep[name] = a
             return a.ctypes.data
 
@@ -229,6 +239,7 @@ class OracleModel:
             m.wgate[l] = ptr(p + "ffn_gate.weight", np.uint16)
             m.wup[l] = ptr(p + "ffn_up.weight", np.uint16)
             m.wdown[l] = ptr(p + "ffn_down.weight", np.uint16)
+        m.f32 = 1 if f32 else 0
         self.m = m
         self.state = lib().or_state_create(ctypes.byref(m))
         if not self.state:

@@ -96,3 +96,19 @@ def test_oracle_gemv_close_to_f64(oracle):
     y = oracle.gemv_f16(W, x)
     ref = W.astype(np.float64) @ x.astype(np.float64)
     assert np.abs(y - ref).max() < 1e-4
+
+
+def test_oracle_f32_storage_mode_matches_f16(oracle, tiny_weights):
+    """WeightStorageModeComparisonTest (integration/WeightStorageModeComparisonTest.java:23-84)
+    asserts that F16, F16_FAST and F32 storage give bit-identical logits: the
+    F32 mode widens the same F16 values exactly and the GEMV sums the same
+    products in the same order.  Checked on the synthetic model."""
+    cfg, w = tiny_weights
+    m16 = oracle.OracleModel(cfg, w)
+    m32 = oracle.OracleModel(cfg, w, f32=True)
+    for pos, t in enumerate([5, 77, 3, 900]):
+        assert np.array_equal(m16.forward(t, pos), m32.forward(t, pos))
+    w32 = {k: (v.astype(np.float32) if v.dtype == np.float16 else v) for k, v in w.items()}
+    m32b = oracle.OracleModel(cfg, w32, f32=True)  # F32 tensors as given
+    m16.forward(5, 0)
+    assert np.array_equal(m16.forward(6, 1), (m32b.forward(5, 0), m32b.forward(6, 1))[1])

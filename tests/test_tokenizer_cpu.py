@@ -231,3 +231,23 @@ def test_gguf_tokenizer_metadata(tmp_path):
     assert tk.decode(tk.encode("Say hi")) == "Say hi"
     with pytest.raises(ValueError):
         write_gguf(path, cfg, w, tokenizer=(toks[:10], merges))
+
+
+def test_gguf_f32_projections_round_trip(tmp_path):
+    """F32 projection tensors are written as GGML type F32 and read back
+    bit-exact (LlamaModel.mapTensor's F32 branch); other dtypes are refused."""
+    from llamahat.config import LlamaConfig
+    from llamahat.gguf import read_gguf, write_gguf
+    from llamahat.synth import synth_weights
+    cfg = LlamaConfig(dim=64, hidden=128, n_layers=1, n_heads=2, n_kv_heads=1, head_dim=32, vocab=1000, max_seq=32)
+    w = {k: (v.astype(np.float32) + np.float32(1e-5)) if v.dtype == np.float16 else v
+         for k, v in synth_weights(cfg, seed=4).items()}
+    path = str(tmp_path / "f32.gguf")
+    write_gguf(path, cfg, w)
+    _, t = read_gguf(path)
+    for k, v in w.items():
+        assert t[k].dtype == np.float32 and np.array_equal(np.asarray(t[k]).reshape(v.shape), v), k
+    bad = dict(w)
+    bad["output_norm.weight"] = bad["output_norm.weight"].astype(np.float16)
+    with pytest.raises(TypeError):
+        write_gguf(path, cfg, bad)

@@ -17,12 +17,14 @@
 // the CTA's whole multi-step tile schedule and moves 8-row weight tiles
 // (layout in lc_internal.h) into a ring of shared-memory stages with 1-D bulk
 // copies; it never waits for activations, so HBM keeps streaming while the
-// consumer warps exchange data with the other CTAs.  Eight consumer warps
-// each own a fixed column slice of every tile: the activation slice sits in
-// registers as f16 hi/lo pairs (x*2^e = hi + lo to 2^-22, exact products)
-// and the tile rows come in with ldmatrix, so a tile costs a warp a handful
-// of mma.sync m16n8k16 with fp32 accumulation.  Per-warp partial sums meet in
-// shared memory and the job epilogue adds them in a fixed order.
+// consumer warps exchange data with the other CTAs.  A mover thread copies
+// each landed tile into a ring of tensor-memory slots (tcgen05.cp), which
+// frees the stage and adds the 256 KB of TMEM to the data in flight per SM.
+// Eight consumer warps each read a fixed share of every tile with
+// tcgen05.ld: 64 weights of one row against 64 fp32 inputs held in registers
+// for the whole job, exact fp32 products on the FMA pipe.  Per-warp partial
+// sums meet in shared memory and the job epilogue adds them in a fixed
+// order.
 //
 // Exchanges: x (after O and DN), q, this position's k and v, the attention
 // outputs and partials and the argmax candidates travel as 64-bit words
@@ -517,9 +519,10 @@ __device__ __forceinline__ bool gather_tagged(const DecodeParams& p, const uint6
 #pragma unroll
     for (int k = 0; k < NV; ++k) stale = stale || !fresh[k];
     if (!stale) return true;
+    // No sleep between rounds: each round is one L2 round trip already
+    // (measured 3.5 us per 1B forward faster than a 128 ns back-off).
     const uint64_t deadline = globaltimer_ns() + p.timeout_ns;
     for (uint32_t it = 1;; ++it) {
-        __nanosleep(128);
 #pragma unroll
         for (int k = 0; k < NV; ++k) {
             if (!fresh[k]) {
@@ -1234,6 +1237,8 @@ __device__ __forceinline__ bool run_attention(const DecodeParams& p, const Smem&
 __device__ __forceinline__ bool stage_h(const DecodeParams& p, const Smem& sm, uint32_t want, Tracer& tr) {
     // h is plain fp32 (half the bytes of tagged words): the gate/up
     // epilogues publish it with a fence, the flags are read with acquire.
+    // (Tagged h measured slower: 639 against 598 us per 1B forward, and 666
+    // with the flags polled first; the fence costs about 1.5 us per layer.)
     constexpr int NV = 8;  // float4 per thread: hidden <= 8 * 4 * kCT (decode_plan)
     const bool ok = wait_flags(p, want, all_ctas(), true);
     tr.mark();

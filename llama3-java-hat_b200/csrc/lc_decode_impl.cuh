@@ -399,7 +399,8 @@ __device__ __forceinline__ bool stage_store(const Smem& sm, const float4 (&v)[NV
 // tile's slot (m < 16, cc < 8).  Consumer warp w reads the lanes of its
 // quarter q = w % 4 (m = 4 q + lane / 8, row r = lane % 8) and the slot's
 // columns [2 KS h, 2 KS (h + 1)), h = w / 4: 2 KS words = 4 KS halves of one
-// row, whose input columns are fixed per thread -- the x segment below.
+// row, whose input columns are fixed per thread (xs_col; dot_share reads them
+// from the staged vector).
 
 // Input column of half e (0, 1) of word k of the thread's share of a tile.
 template <int KS>
@@ -407,19 +408,6 @@ __device__ __forceinline__ int xs_col(int k, int e) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m = 4 * (warp & 3) + (lane >> 3), c = 2 * KS * (warp >> 2) + k;
     return 256 * (c >> 3) + 16 * m + 2 * (c & 7) + e;
-}
-
-// The thread's x segment of column block cb (4 KS floats) from act.
-template <int KS>
-__device__ __forceinline__ void build_xs(const Smem& sm, int col0, float (&xs)[4 * KS]) {
-#pragma unroll
-    for (int k = 0; k < 2 * KS; k += 2) {
-        const float4 v = *reinterpret_cast<const float4*>(sm.act + col0 + xs_col<KS>(k, 0));
-        xs[2 * k] = v.x;
-        xs[2 * k + 1] = v.y;
-        xs[2 * k + 2] = v.z;
-        xs[2 * k + 3] = v.w;
-    }
 }
 
 // 2 KS consecutive 32-bit TMEM columns of the warp's 32 lanes (thread i:
@@ -455,16 +443,34 @@ __device__ __forceinline__ void tmem_ld_share(uint32_t taddr, uint32_t (&v)[2 * 
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// d0 = fma(a0, b0, d0) and d1 = fma(a1, b1, d1), each an IEEE fma.rn, issued
+// as one packed instruction (fma.rn.f32x2, sm_100a).
+__device__ __forceinline__ void fma_pair(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 pa, pb, pc;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\tmov.b64 pc, {%0, %1};\n\t"
+        "fma.rn.f32x2 pc, pa, pb, pc;\n\tmov.b64 {%0, %1}, pc;\n\t}"
+        : "+f"(d0), "+f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // The thread's partial dot product over its share of one tile: exact
-// products of the F16 weights with the fp32 inputs, four fp32 chains.
+// products of the F16 weights with the fp32 inputs, four fp32 chains (word k
+// of the share feeds chains 0, 1 when k is even and 2, 3 when k is odd), two
+// of them advanced per packed FMA.  The inputs are read from the staged
+// vector in shared memory (xrow: act at the column block's first column), a
+// float4 per pair of words: the eight lanes of a row quarter read the same
+// four floats, so a warp's load is four broadcast addresses.  Holding the
+// 4 KS inputs in registers instead cost spills, and with them most of the
+// consumers' time per tile.
 template <int KS>
-__device__ __forceinline__ float dot_share(const uint32_t (&v)[2 * KS], const float (&xs)[4 * KS]) {
+__device__ __forceinline__ float dot_share(const uint32_t (&v)[2 * KS], const float* xrow) {
     float a[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int k = 0; k < 2 * KS; ++k) {
-        const float2 w = __half22float2(*reinterpret_cast<const __half2*>(&v[k]));
-        a[(2 * k) & 3] = fmaf(w.x, xs[2 * k], a[(2 * k) & 3]);
-        a[(2 * k + 1) & 3] = fmaf(w.y, xs[2 * k + 1], a[(2 * k + 1) & 3]);
+    for (int k = 0; k < 2 * KS; k += 2) {
+        const float4 x = *reinterpret_cast<const float4*>(xrow + xs_col<KS>(k, 0));
+        const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&v[k]));
+        const float2 w1 = __half22float2(*reinterpret_cast<const __half2*>(&v[k + 1]));
+        fma_pair(a[0], a[1], w0.x, w0.y, x.x, x.y);
+        fma_pair(a[2], a[3], w1.x, w1.y, x.z, x.w);
     }
     return (a[0] + a[1]) + (a[2] + a[3]);
 }
@@ -928,8 +934,7 @@ __device__ __forceinline__ RingPos consume_batch(const DecodeParams& p, RingPos 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, ng = b1 - b0;
     const uint32_t tbase = sm.sh->tmem + ((uint32_t)(32 * (warp & 3)) << 16) + 2u * KS * (uint32_t)(warp >> 2);
     for (int cb = 0; cb < ncb; ++cb) {
-        float xs[4 * KS];
-        build_xs<KS>(sm, cb * p.dim, xs);
+        const float* xrow = sm.act + cb * p.dim;
 #pragma unroll 1
         for (int g = b0; g < b1; ++g) {
             const unsigned long long t0 = timing ? globaltimer_ns() : 0ull;
@@ -949,7 +954,7 @@ __device__ __forceinline__ RingPos consume_batch(const DecodeParams& p, RingPos 
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sm.tempty[r.slot]);
-                y = dot_share<KS>(v, xs);
+                y = dot_share<KS>(v, xrow);
             } else {
                 r.ok = 0;
             }

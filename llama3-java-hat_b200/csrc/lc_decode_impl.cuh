@@ -366,20 +366,6 @@ __device__ __forceinline__ void run_mover(const DecodeParams& p, const Smem& sm)
 
 // ------------------------------------------------------- consumer helpers --
 
-__device__ __forceinline__ void ldsm4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr)
-                 : "memory");
-}
-
-// D += A * B, m16n8k16, f16 inputs, fp32 accumulation.
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
 // The staged GEMV input in act, fp32: the thread's values v[k] are the
 // float4 at index idx[k] of the vector (idx < 0: none).  Ends with a barrier
 // that also makes `ok` (the thread's status so far) CTA-uniform.

@@ -136,8 +136,10 @@ cudaError_t launch_keyx(const KeyxArgs& a, cudaStream_t st, bool pdl);
 // [CB / 8 column octets][8 rows][8 halves] (16 * CB bytes, contiguous), and
 // tile (g, cb) of a matrix with ncb = cols / CB column blocks starts at
 // element (g * ncb + cb) * 8 * CB.  One 1-D bulk copy moves a tile into
-// shared memory, where the 8x8 half blocks feed ldmatrix without bank
-// conflicts.  Rows are padded to a multiple of 8 with zeros.
+// shared memory, where each 8x8 block of halves (128 contiguous bytes) is a
+// core matrix of a K-major, no-swizzle tcgen05 descriptor, so tcgen05.cp
+// moves the tile into tensor memory as it lies.  Rows are padded to a
+// multiple of 8 with zeros.
 struct LayerW {
     const __half* wqkv;   // tiled [dim + 2*kv_dim][dim]
     const __half* wo;     // tiled [dim][n_heads*head_dim]

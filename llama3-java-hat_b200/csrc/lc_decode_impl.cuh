@@ -66,6 +66,7 @@ static_assert(kCT * kRegConsumer + 128 * kRegProducer <= kThreads * kRegLaunch, 
 constexpr uint32_t kBarC = 1;         // named barrier of the consumer threads
 constexpr uint32_t kBarEnd = 6;       // consumers + the mover warp, before the TMEM is freed (2..5: attention pairs)
 constexpr int kBatchTiles = 8;        // tiles per epilogue batch
+constexpr int kBatchTilesWide = 16;   // ... of a job with one column block (partials past 8 tiles in act)
 constexpr int kMaxStages = 24;
 // Five 32 KB stages at dim 2048: the plan then fits the 196 KB shared-memory
 // carveout and leaves 60 KB of L1 for the attention and activation loads
@@ -121,6 +122,8 @@ struct Shared {
 // 1024-aligned base), all compile-time constants: act holds the largest GEMV
 // input (h, up to kActFloats floats) or the attention scratch.
 constexpr int kActFloats = 8192;
+static_assert(2048 + (kBatchTilesWide - kBatchTiles) * 8 * kCW <= kActFloats,
+              "the wide batches' partials must fit in act beside an input of dim <= 2048 floats");
 struct Layout {
     int tile_bytes, stages;
     int off_bar, off_sh, off_act, off_ys, total;
@@ -185,8 +188,12 @@ __host__ __device__ __forceinline__ JobGeo job_geo(const DecodeParams& p, const 
     }
 }
 
-// Groups of a batch: at most kBatchTiles tiles, column-block-major inside.
+// Groups of a batch: at most kBatchTiles tiles, column-block-major inside;
+// jobs of one column block take kBatchTilesWide (their input fills only dim
+// floats of act, and the partials of the tiles past kBatchTiles go there).
+// With one column block the tile order does not depend on the batch size.
 __host__ __device__ __forceinline__ int batch_groups(int ncb) {
+    if (ncb == 1) return kBatchTilesWide;
     const int b = kBatchTiles / ncb;
     return b < 1 ? 1 : b;
 }
@@ -776,12 +783,19 @@ __device__ __forceinline__ bool stage_att(const DecodeParams& p, const Smem& sm,
     return stage_store<2>(sm, v, idx, ok);
 }
 
+// Partials of tile t of a batch: [8 rows][kCW warps] floats.  Tiles past
+// kBatchTiles (wide batches of one-column-block jobs, whose input takes the
+// first dim floats of act) use act after the input.
+__device__ __forceinline__ float* ys_tile(const Smem& sm, int dim, int t) {
+    return t < kBatchTiles ? sm.ys + t * 8 * kCW : sm.act + dim + (t - kBatchTiles) * 8 * kCW;
+}
+
 // Sum over column blocks and warps of row r (0..7) of group gg of a batch of
 // ng groups, fixed order.
-__device__ __forceinline__ float row_sum(const float* ys, int ng, int ncb, int gg, int r) {
+__device__ __forceinline__ float row_sum(const Smem& sm, int dim, int ng, int ncb, int gg, int r) {
     float y = 0.0f;
     for (int cb = 0; cb < ncb; ++cb) {
-        const float4* v = reinterpret_cast<const float4*>(ys + ((cb * ng + gg) * 8 + r) * kCW);
+        const float4* v = reinterpret_cast<const float4*>(ys_tile(sm, dim, cb * ng + gg) + r * kCW);
         const float4 a = v[0], b = v[1];
         y += ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w));
     }
@@ -817,7 +831,7 @@ __device__ __forceinline__ void epilogue(const DecodeParams& p, const Smem& sm, 
     if (kind == kQKV) {
         for (int pi = tid; pi < nrows / 2; pi += kCT) {
             const int gg = pi >> 2, r = (pi & 3) * 2, R = (b0 + gg) * 8 + r;
-            float y0 = row_sum(sm.ys, ng, 1, gg, r), y1 = row_sum(sm.ys, ng, 1, gg, r + 1);
+            float y0 = row_sum(sm, p.dim, ng, 1, gg, r), y1 = row_sum(sm, p.dim, ng, 1, gg, r + 1);
             // q rows, then k rows, then v rows; k and q are rotated.
             const int kv = R < qdim ? -1 : (R < qdim + kvd ? 0 : 1);
             const int rr = R - (kv < 0 ? 0 : qdim + kv * kvd), i = rr & (HD - 1);
@@ -836,15 +850,16 @@ __device__ __forceinline__ void epilogue(const DecodeParams& p, const Smem& sm, 
         // rows 4m..4m+3 = (gate, up) of h[2m], h[2m+1] (TransformerBlock.java:205-209)
         for (int pi = tid; pi < nrows / 4; pi += kCT) {
             const int gg = pi >> 1, r = (pi & 1) * 4, R = (b0 + gg) * 8 + r;
-            const float h0 = __fmul_rn(silu_f(row_sum(sm.ys, ng, 1, gg, r)), row_sum(sm.ys, ng, 1, gg, r + 1));
-            const float h1 = __fmul_rn(silu_f(row_sum(sm.ys, ng, 1, gg, r + 2)), row_sum(sm.ys, ng, 1, gg, r + 3));
+            const float h0 = __fmul_rn(silu_f(row_sum(sm, p.dim, ng, 1, gg, r)), row_sum(sm, p.dim, ng, 1, gg, r + 1));
+            const float h1 =
+                __fmul_rn(silu_f(row_sum(sm, p.dim, ng, 1, gg, r + 2)), row_sum(sm, p.dim, ng, 1, gg, r + 3));
             *reinterpret_cast<float2*>(p.h + (R >> 1)) = make_float2(h0, h1);
         }
     } else if (kind == kLM) {
         for (int k = tid; k < nrows; k += kCT) {
             const int R = b0 * 8 + k;
             if (R < p.vocab) {
-                const float v = row_sum(sm.ys, ng, 1, k >> 3, k & 7);
+                const float v = row_sum(sm, p.dim, ng, 1, k >> 3, k & 7);
                 p.logits[R] = v;
                 if (R == 0 && v != v) lm.nan0 = true;
                 if (v == v && (lm.bi < 0 || v > lm.bv)) {
@@ -855,7 +870,7 @@ __device__ __forceinline__ void epilogue(const DecodeParams& p, const Smem& sm, 
         }
     } else if (tid < nrows) {  // O, DN: residual add (TransformerBlock.java:195-198, 211-216)
         uint64_t* out = (kind == kO) ? p.xa : p.xb;
-        st_tag1(out + b0 * 8 + tid, __fadd_rn(res, row_sum(sm.ys, ng, ncb, tid >> 3, tid & 7)), tg);
+        st_tag1(out + b0 * 8 + tid, __fadd_rn(res, row_sum(sm, p.dim, ng, ncb, tid >> 3, tid & 7)), tg);
     }
 }
 
@@ -946,7 +961,7 @@ __device__ __forceinline__ RingPos consume_batch(const DecodeParams& p, RingPos 
             }
             y += __shfl_xor_sync(0xffffffffu, y, 8);
             y += __shfl_xor_sync(0xffffffffu, y, 16);
-            if (lane < 8) sm.ys[((cb * ng + (g - b0)) * 8 + lane) * kCW + warp] = y;
+            if (lane < 8) ys_tile(sm, p.dim, cb * ng + (g - b0))[lane * kCW + warp] = y;
             if (++r.slot == kSlots) {
                 r.slot = 0;
                 r.par ^= 1u;

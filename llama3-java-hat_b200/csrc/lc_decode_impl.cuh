@@ -571,21 +571,6 @@ __device__ __forceinline__ FlagSet all_ctas() {
     return f;
 }
 
-// Rank (job_range with unit 1) that owns group g of a job with P groups.
-__device__ __forceinline__ int owner_rank(int P, int G, int g) {
-    const int base = P / G, ext = P % G;
-    if (g < ext * (base + 1)) return g / (base + 1);
-    return ext + (g - ext * (base + 1)) / base;
-}
-
-// The CTAs that run the attention units of a position with nsplit splits per
-// kv head (unit u runs on CTA u * G / units).
-__device__ __forceinline__ FlagSet attn_ctas(const DecodeParams& p, int nsplit) {
-    FlagSet f = all_ctas();
-    f.units = p.n_kv * nsplit;
-    return f;
-}
-
 // Warp 0 polls the flags of the set until all reached `want` (bounded); the
 // barrier (and with `acquire` a fence) orders the CTA's later loads after the
 // flags.  Each lane polls at most kPollPerLane flags, all loads of a round in
